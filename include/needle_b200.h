@@ -1,0 +1,177 @@
+/*
+ * needle_b200 -- C ABI of the B200 (sm_100a) attention hot path for needle.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes,
+ * plus the CUDA stream to launch on (a cudaStream_t passed as void*; NULL is
+ * the legacy default stream).  Nothing here synchronises the device except
+ * nb_device_errors().  Shapes, dtypes and strides are validated on the host
+ * and reported as a non-zero status with a message from nb_last_error();
+ * nothing is launched in that case.  Kernels never trap: a block id outside
+ * the pool or an invalid position is skipped and recorded in a device-side
+ * error word that nb_device_errors() returns.
+ *
+ * Tensor layouts are needle's:
+ *   kv_cache     [2, num_blocks, num_kv_heads, block_size, head_dim], dense
+ *                (needle/model/runner.py:65-78); index 0 is K, 1 is V.
+ *   block_table  [num_seqs, max_blocks_per_seq] int32, row stride given
+ *                (needle/model/runner.py:220-235, padded with the last block).
+ *   cu_seqlens   [num_seqs + 1] int32 prefix sums of new tokens per sequence.
+ *   context_lens [num_seqs] int32, tokens already in the cache
+ *                (needle/model/runner.py:204-218).
+ * Token-major activations ([T, heads, head_dim]) take a row stride in
+ * elements between consecutive tokens; heads are head_dim elements apart.
+ */
+#ifndef NEEDLE_B200_H
+#define NEEDLE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NB_API __attribute__((visibility("default")))
+#else
+#define NB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define NB_OK 0
+#define NB_ERR_INVALID_ARG 1
+#define NB_ERR_UNSUPPORTED 2
+#define NB_ERR_CUDA 3
+
+/* element types */
+#define NB_DTYPE_F32 0
+#define NB_DTYPE_F16 1
+#define NB_DTYPE_BF16 2
+
+/* bits of the device error word */
+#define NB_DEVERR_BLOCK_ID 1u /* a block-table entry outside [0, num_blocks) */
+#define NB_DEVERR_POSITION 2u /* a negative context length / position */
+#define NB_DEVERR_TIMEOUT 4u  /* a bounded wait on an async copy ran out */
+
+/* ABI version of this header (bumped on any signature change). */
+NB_API int nb_abi_version(void);
+
+/* Message of the last non-zero status returned on this thread. */
+NB_API const char* nb_last_error(void);
+
+/* Synchronises the current device, returns the device error word in
+ * *flags_out and clears it.  Returns NB_ERR_CUDA if the device is in error. */
+NB_API int nb_device_errors(unsigned* flags_out);
+
+/*
+ * Scatter new K/V tokens into the paged cache.
+ * Replaces needle/layers/attention.py:204-246 (_write_kv, prefill) and
+ * needle/layers/attention.py:140-154 (the decode KV write).
+ * Token i of sequence s goes to position context_lens[s] + i; its block-table
+ * column is position / block_size clamped to max_blocks_per_seq - 1 (:235);
+ * when the clamp makes several tokens of one sequence share a slot the last
+ * one wins.  cu_seqlens == NULL means one token per sequence (decode):
+ * num_tokens must then equal num_seqs.  Byte-exact copy.
+ */
+NB_API int nb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                     void* kv_cache, int num_blocks, int num_kv_heads, int block_size,
+                     int head_dim, const int32_t* block_table, int64_t block_table_stride,
+                     int max_blocks_per_seq, const int32_t* cu_seqlens,
+                     const int32_t* context_lens, int num_seqs, int num_tokens, int dtype,
+                     void* stream);
+
+/*
+ * In-place NeoX rotary embedding of q [T, num_q_heads, D] and k
+ * [T, num_kv_heads, D] with per-token tables cos/sin [T, D] (row stride
+ * cs_stride).  Replaces needle/layers/attention.py:277-288 (_apply_rope):
+ * x*cos + rotate_half(x)*sin with the result of each multiply and of the add
+ * rounded to the storage dtype, so the output is bit-identical to the
+ * reference.  k may be NULL (num_kv_heads ignored).
+ */
+NB_API int nb_rope(void* q, int64_t q_stride, int num_q_heads, void* k, int64_t k_stride,
+            int num_kv_heads, const void* cos, const void* sin, int64_t cs_stride, int num_tokens,
+            int head_dim, int dtype, void* stream);
+
+/*
+ * nb_rope followed by nb_store_kvcache in one launch: q is rotated in place,
+ * k is rotated and written to the cache (and back into k when
+ * write_k_back != 0), v is copied to the cache.  Replaces the sequence
+ * needle/layers/attention.py:88 (_apply_rope) + :140-154 or :204-246.
+ */
+NB_API int nb_rope_store_kvcache(void* q, int64_t q_stride, int num_q_heads, void* k, int64_t k_stride,
+                          const void* v, int64_t v_stride, const void* cos, const void* sin,
+                          int64_t cs_stride, void* kv_cache, int num_blocks, int num_kv_heads,
+                          int block_size, int head_dim, const int32_t* block_table,
+                          int64_t block_table_stride, int max_blocks_per_seq,
+                          const int32_t* cu_seqlens, const int32_t* context_lens, int num_seqs,
+                          int num_tokens, int write_k_back, int dtype, void* stream);
+
+/*
+ * Split-K plan for nb_paged_decode: pages (KV blocks) per split and the
+ * number of splits per sequence that the workspace must hold, chosen from
+ * the batch shape and the block-table width only (no device reads).
+ */
+NB_API int nb_paged_decode_plan(int num_seqs, int num_kv_heads, int max_blocks_per_seq, int block_size,
+                         int* pages_per_split, int* max_splits);
+
+/* Bytes of workspace nb_paged_decode needs for this shape and split count. */
+NB_API size_t nb_paged_decode_workspace_size(int num_seqs, int num_q_heads, int head_dim,
+                                      int max_splits);
+
+/*
+ * Paged decode attention: for every sequence s and query head j, attention
+ * of q[s, j] over the first context_lens[s] + 1 cached tokens of KV head
+ * j / (num_q_heads / num_kv_heads), scaled by `scale`.
+ * Replaces needle/layers/attention.py:291-310 (_decode_pytorch) and
+ * :161-197 (_decode_flashinfer).  Split-K: each split of pages_per_split
+ * pages is one CTA per (split, kv head, sequence) writing fp32 partials to
+ * `workspace`; a separate merge kernel combines the splits.  Any group size
+ * num_q_heads / num_kv_heads (power of two or not) is supported.
+ * The caller allocates the workspace (nb_paged_decode_workspace_size).
+ */
+NB_API int nb_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                    const void* kv_cache, int num_blocks, int num_kv_heads, int block_size,
+                    int head_dim, int num_q_heads, const int32_t* block_table,
+                    int64_t block_table_stride, int max_blocks_per_seq,
+                    const int32_t* context_lens, int num_seqs, float scale, void* out,
+                    int64_t out_stride_seq, int64_t out_stride_head, void* workspace,
+                    size_t workspace_bytes, int pages_per_split, int dtype, void* stream);
+
+/*
+ * Causal prefill attention over each sequence's new tokens, q [T, Hq, D],
+ * k/v [T, Hkv, D] (post-RoPE, token-major, row strides given), output
+ * [T, Hq, D].  Replaces needle/layers/attention.py:120-134 (_prefill_pytorch)
+ * and :109-118 (_prefill_flashinfer): within sequence s token i attends to
+ * tokens 0..i of the same sequence, query head j to KV head j / group.
+ */
+NB_API int nb_prefill_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                         const void* v, int64_t v_stride, int num_q_heads, int num_kv_heads,
+                         int head_dim, const int32_t* cu_seqlens, int num_seqs, int num_tokens,
+                         int max_seqlen, float scale, void* out, int64_t out_stride, int dtype,
+                         void* stream);
+
+/*
+ * RMSNorm of x [T, hidden]: y = weight * (x * rsqrt(mean(x^2) + eps)), with
+ * the mean of squares in fp32 and the rounding points of
+ * needle/layers/norm.py:14-17.
+ */
+NB_API int nb_rmsnorm(const void* x, int64_t x_stride, const void* weight, void* out,
+               int64_t out_stride, int num_tokens, int hidden, float eps, int dtype,
+               void* stream);
+
+/*
+ * Residual add fused with RMSNorm: h = residual + x (rounded to dtype),
+ * residual_out = h, out = RMSNorm(h).  Replaces the decoder-layer sequence
+ * needle/model/llama.py:67-70 (and :72 + the next layer's :62).
+ * residual_out may alias residual; out may alias x.
+ */
+NB_API int nb_fused_add_rmsnorm(const void* x, int64_t x_stride, const void* residual,
+                         int64_t residual_stride, const void* weight, void* out,
+                         int64_t out_stride, void* residual_out, int64_t residual_out_stride,
+                         int num_tokens, int hidden, float eps, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEEDLE_B200_H */

@@ -1,0 +1,264 @@
+"""Torch-facing wrappers over the C ABI (``include/needle_b200.h``).
+
+Each function takes CUDA tensors in needle's layouts, checks dtypes and
+shapes, and launches on torch's current stream.  There is no CPU or
+library fallback: a CPU tensor, an unsupported dtype or a missing library
+raises.  Nothing here synchronises the device.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.NB_DTYPE_F32, torch.float16: L.NB_DTYPE_F16,
+       torch.bfloat16: L.NB_DTYPE_BF16}
+
+
+def _dtype(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"needle_b200: unsupported dtype {t.dtype}") from None
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("needle_b200 ops take CUDA tensors (there is no CPU path)")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _rows(t: torch.Tensor, name: str) -> int:
+    """Row stride of a token-major [T, heads, D] (or [T, heads*D]) tensor whose
+    heads are dense within a row."""
+    if t.dim() == 3:
+        if t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+            raise ValueError(f"{name}: heads must be dense within a token row")
+    elif t.dim() == 2:
+        if t.stride(1) != 1:
+            raise ValueError(f"{name}: last dim must be contiguous")
+    else:
+        raise ValueError(f"{name}: expected a [T, heads, D] tensor")
+    return t.stride(0)
+
+
+def _i32(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.int32:
+        raise TypeError(f"{name} must be int32 (got {t.dtype})")
+    return t
+
+
+def _cache_dims(kv_cache: torch.Tensor):
+    if kv_cache.dim() != 5 or kv_cache.shape[0] != 2 or not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous [2, num_blocks, kv_heads, block_size, D] tensor")
+    _, n, kvh, bs, d = kv_cache.shape
+    return n, kvh, bs, d
+
+
+def _bt(block_table: torch.Tensor):
+    _i32(block_table, "block_table")
+    if block_table.dim() != 2 or block_table.stride(1) != 1:
+        raise ValueError("block_table must be [num_seqs, max_blocks] with unit column stride")
+    return block_table.stride(0), block_table.shape[1]
+
+
+# --------------------------------------------------------------------------
+# KV cache writes and RoPE
+# --------------------------------------------------------------------------
+
+def store_kvcache(k: torch.Tensor, v: torch.Tensor, kv_cache: torch.Tensor,
+                  block_table: torch.Tensor, context_lens: torch.Tensor,
+                  cu_seqlens: Optional[torch.Tensor] = None) -> None:
+    """Scatter ``k``/``v`` ``[T, kv_heads, D]`` into the paged cache in place.
+
+    ``cu_seqlens=None`` is the decode case (one token per sequence).
+    """
+    _cuda(k, v, kv_cache, block_table, context_lens, cu_seqlens)
+    n, kvh, bs, d = _cache_dims(kv_cache)
+    bts, maxb = _bt(block_table)
+    _i32(context_lens, "context_lens")
+    if cu_seqlens is not None:
+        _i32(cu_seqlens, "cu_seqlens")
+    dt = _dtype(kv_cache)
+    if k.dtype != kv_cache.dtype or v.dtype != kv_cache.dtype:
+        raise TypeError("k/v dtype must match the cache")
+    L.check(L.lib().nb_store_kvcache(
+        k.data_ptr(), _rows(k, "k"), v.data_ptr(), _rows(v, "v"), kv_cache.data_ptr(),
+        n, kvh, bs, d, block_table.data_ptr(), bts, maxb,
+        cu_seqlens.data_ptr() if cu_seqlens is not None else None,
+        context_lens.data_ptr(), context_lens.shape[0], k.shape[0], dt, _stream(k)))
+
+
+def rope_(q: torch.Tensor, k: Optional[torch.Tensor], cos: torch.Tensor,
+          sin: torch.Tensor) -> None:
+    """In-place NeoX RoPE of ``q [T, Hq, D]`` and ``k [T, Hkv, D]``."""
+    _cuda(q, k, cos, sin)
+    dt = _dtype(q)
+    if cos.dtype != q.dtype or sin.dtype != q.dtype:
+        raise TypeError("cos/sin dtype must match q")
+    if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
+        raise ValueError("cos/sin must share a row stride with unit column stride")
+    T, hq, d = q.shape
+    L.check(L.lib().nb_rope(
+        q.data_ptr(), _rows(q, "q"), hq,
+        k.data_ptr() if k is not None else None, _rows(k, "k") if k is not None else 0,
+        k.shape[1] if k is not None else 0,
+        cos.data_ptr(), sin.data_ptr(), cos.stride(0), T, d, dt, _stream(q)))
+
+
+def rope_store_kvcache(q, k, v, cos, sin, kv_cache, block_table, context_lens,
+                       cu_seqlens=None, write_k_back: bool = False) -> None:
+    """RoPE on ``q`` (in place) and ``k``, then K/V into the cache, one launch."""
+    _cuda(q, k, v, cos, sin, kv_cache, block_table, context_lens, cu_seqlens)
+    n, kvh, bs, d = _cache_dims(kv_cache)
+    bts, maxb = _bt(block_table)
+    _i32(context_lens, "context_lens")
+    dt = _dtype(kv_cache)
+    for t in (q, k, v, cos, sin):
+        if t.dtype != kv_cache.dtype:
+            raise TypeError("q/k/v/cos/sin dtype must match the cache")
+    if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
+        raise ValueError("cos/sin must share a row stride with unit column stride")
+    L.check(L.lib().nb_rope_store_kvcache(
+        q.data_ptr(), _rows(q, "q"), q.shape[1], k.data_ptr(), _rows(k, "k"),
+        v.data_ptr(), _rows(v, "v"), cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+        kv_cache.data_ptr(), n, kvh, bs, d, block_table.data_ptr(), bts, maxb,
+        cu_seqlens.data_ptr() if cu_seqlens is not None else None, context_lens.data_ptr(),
+        context_lens.shape[0], q.shape[0], int(bool(write_k_back)), dt, _stream(q)))
+
+
+# --------------------------------------------------------------------------
+# Paged decode
+# --------------------------------------------------------------------------
+
+class DecodePlan:
+    """Split-K plan plus workspace for one decode step.
+
+    Built once per step from host-known shapes (batch, KV heads, block-table
+    width) and reused by every layer of the step: the workspace is consumed
+    by each layer's merge before the next layer's decode runs on the same
+    stream.
+    """
+
+    def __init__(self, num_seqs: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                 max_blocks: int, block_size: int, device, pages_per_split: Optional[int] = None):
+        lib = L.lib()
+        if pages_per_split is None:
+            import ctypes
+            pps, ms = ctypes.c_int(0), ctypes.c_int(0)
+            L.check(lib.nb_paged_decode_plan(num_seqs, num_kv_heads, max_blocks, block_size,
+                                             ctypes.byref(pps), ctypes.byref(ms)))
+            pages_per_split = pps.value
+        self.pages_per_split = int(pages_per_split)
+        self.max_splits = -(-max_blocks // self.pages_per_split)
+        nbytes = lib.nb_paged_decode_workspace_size(num_seqs, num_q_heads, head_dim,
+                                                    self.max_splits)
+        self.workspace = (torch.empty(nbytes, dtype=torch.uint8, device=device)
+                          if nbytes else None)
+        self.key = (num_seqs, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size)
+
+
+def paged_decode(q: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
+                 context_lens: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
+                 plan: Optional[DecodePlan] = None) -> torch.Tensor:
+    """Decode attention of ``q [B, Hq, D]`` over ``context_lens + 1`` cached
+    tokens per sequence.  Returns ``out [B, Hq, D]``."""
+    _cuda(q, kv_cache, block_table, context_lens, out)
+    n, kvh, bs, d = _cache_dims(kv_cache)
+    bts, maxb = _bt(block_table)
+    _i32(context_lens, "context_lens")
+    if q.dtype != kv_cache.dtype:
+        raise TypeError("q dtype must match the cache")
+    B, hq, qd = q.shape
+    if qd != d or q.stride(2) != 1:
+        raise ValueError("q must be [B, Hq, D] with unit last stride")
+    if out is None:
+        out = torch.empty((B, hq, d), dtype=q.dtype, device=q.device)
+    if plan is None or plan.key != (B, hq, kvh, d, maxb, bs):
+        plan = DecodePlan(B, hq, kvh, d, maxb, bs, q.device)
+    ws = plan.workspace
+    L.check(L.lib().nb_paged_decode(
+        q.data_ptr(), q.stride(0), q.stride(1), kv_cache.data_ptr(), n, kvh, bs, d, hq,
+        block_table.data_ptr(), bts, maxb, context_lens.data_ptr(), B, float(scale),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        plan.pages_per_split, _dtype(q), _stream(q)))
+    return out
+
+
+# --------------------------------------------------------------------------
+# Prefill
+# --------------------------------------------------------------------------
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      cu_seqlens: torch.Tensor, max_seqlen: int, scale: Optional[float] = None,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal attention of each sequence's new tokens; ``[T, Hq, D]`` out."""
+    _cuda(q, k, v, cu_seqlens, out)
+    _i32(cu_seqlens, "cu_seqlens")
+    T, hq, d = q.shape
+    hk = k.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty((T, hq, d), dtype=q.dtype, device=q.device)
+    L.check(L.lib().nb_prefill_attention(
+        q.data_ptr(), _rows(q, "q"), k.data_ptr(), _rows(k, "k"), v.data_ptr(), _rows(v, "v"),
+        hq, hk, d, cu_seqlens.data_ptr(), cu_seqlens.shape[0] - 1, T, int(max_seqlen),
+        float(scale), out.data_ptr(), _rows(out, "out"), _dtype(q), _stream(q)))
+    return out
+
+
+# --------------------------------------------------------------------------
+# RMSNorm
+# --------------------------------------------------------------------------
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _cuda(x, weight, out)
+    if x.stride(-1) != 1 or x.dim() != 2:
+        raise ValueError("x must be [T, hidden] with unit last stride")
+    if weight.dtype != x.dtype or not weight.is_contiguous():
+        raise TypeError("weight must be contiguous with x's dtype")
+    if out is None:
+        out = torch.empty_like(x)
+    T, hid = x.shape
+    L.check(L.lib().nb_rmsnorm(x.data_ptr(), x.stride(0), weight.data_ptr(), out.data_ptr(),
+                               out.stride(0), T, hid, float(eps), _dtype(x), _stream(x)))
+    return out
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                      out: Optional[torch.Tensor] = None,
+                      residual_out: Optional[torch.Tensor] = None
+                      ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``h = residual + x``; returns ``(rmsnorm(h), h)``."""
+    _cuda(x, residual, weight, out, residual_out)
+    for t in (x, residual):
+        if t.stride(-1) != 1 or t.dim() != 2:
+            raise ValueError("x/residual must be [T, hidden] with unit last stride")
+    if residual.dtype != x.dtype or weight.dtype != x.dtype:
+        raise TypeError("dtype mismatch")
+    if out is None:
+        out = torch.empty_like(x)
+    if residual_out is None:
+        residual_out = torch.empty_like(residual)
+    T, hid = x.shape
+    L.check(L.lib().nb_fused_add_rmsnorm(
+        x.data_ptr(), x.stride(0), residual.data_ptr(), residual.stride(0), weight.data_ptr(),
+        out.data_ptr(), out.stride(0), residual_out.data_ptr(), residual_out.stride(0),
+        T, hid, float(eps), _dtype(x), _stream(x)))
+    return out, residual_out
+
+
+def device_errors() -> int:
+    """Synchronise and return (and clear) the device error word; see
+    ``NB_DEVERR_*`` in the header."""
+    return L.device_errors()

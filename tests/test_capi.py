@@ -1,0 +1,94 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+header declares with the declared arity, and rejects invalid arguments on
+the host before touching a device."""
+import ctypes
+import subprocess
+
+import pytest
+
+from needle_b200 import _lib as L
+
+
+def test_header_declares_the_hot_path():
+    decl = L.declared_functions()
+    for name in ("nb_store_kvcache", "nb_rope", "nb_rope_store_kvcache", "nb_paged_decode",
+                 "nb_paged_decode_plan", "nb_paged_decode_workspace_size",
+                 "nb_prefill_attention", "nb_rmsnorm", "nb_fused_add_rmsnorm",
+                 "nb_last_error", "nb_device_errors", "nb_abi_version"):
+        assert name in decl, name
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    for name in L.declared_functions():
+        assert name in exported, f"{name} declared but not exported"
+        assert getattr(lib, name) is not None
+    assert lib.nb_abi_version() == 1
+
+
+def test_no_torch_types_in_signatures():
+    for name, (ret, params) in L.declared_functions().items():
+        for typ, _ in params:
+            assert "Tensor" not in typ and "at::" not in typ, (name, typ)
+
+
+def _err(rc):
+    return rc, L.lib().nb_last_error().decode()
+
+
+def test_invalid_dtype_rejected_on_host():
+    lib = L.lib()
+    rc, msg = _err(lib.nb_store_kvcache(1, 64, 1, 64, 1, 4, 1, 16, 64, 1, 4, 4, None, 1, 1, 1,
+                                        7, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "dtype" in msg
+
+
+def test_store_kvcache_arg_checks():
+    lib = L.lib()
+    # k row stride smaller than kv_heads * head_dim
+    rc, msg = _err(lib.nb_store_kvcache(16, 8, 16, 64, 16, 4, 1, 16, 64, 16, 4, 4, None, 16, 1, 1,
+                                        L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
+    # decode form needs one token per sequence
+    rc, msg = _err(lib.nb_store_kvcache(16, 64, 16, 64, 16, 4, 1, 16, 64, 16, 4, 4, None, 16, 2, 3,
+                                        L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "cu_seqlens" in msg
+    # block table narrower than its declared width
+    rc, msg = _err(lib.nb_store_kvcache(16, 64, 16, 64, 16, 4, 1, 16, 64, 16, 2, 4, None, 16, 1, 1,
+                                        L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG
+
+
+def test_paged_decode_arg_checks():
+    lib = L.lib()
+    # 14 query heads over 3 KV heads is not a grouping
+    rc, msg = _err(lib.nb_paged_decode(16, 14 * 64, 64, 16, 8, 3, 16, 64, 14, 16, 4, 4, 16, 1,
+                                       0.125, 16, 14 * 64, 64, None, 0, 4, L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "multiple" in msg
+    # split-K needs a workspace
+    rc, msg = _err(lib.nb_paged_decode(16, 8 * 64, 64, 16, 8, 2, 16, 64, 8, 16, 16, 16, 16, 2,
+                                       0.125, 16, 8 * 64, 64, None, 0, 4, L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "workspace" in msg
+
+
+def test_decode_plan_and_workspace():
+    lib = L.lib()
+    pps, ms = ctypes.c_int(0), ctypes.c_int(0)
+    assert lib.nb_paged_decode_plan(64, 8, 256, 16, ctypes.byref(pps), ctypes.byref(ms)) == 0
+    assert 1 <= pps.value <= 128 and ms.value == -(-256 // pps.value)
+    assert lib.nb_paged_decode_plan(1, 1, 1, 16, ctypes.byref(pps), ctypes.byref(ms)) == 0
+    assert pps.value == 1 and ms.value == 1
+    assert lib.nb_paged_decode_workspace_size(64, 32, 128, 1) == 0
+    assert lib.nb_paged_decode_workspace_size(64, 32, 128, 3) == 64 * 32 * 3 * (128 * 4 + 8)
+    assert lib.nb_paged_decode_plan(0, 8, 256, 16, ctypes.byref(pps), ctypes.byref(ms)) != 0
+
+
+@pytest.mark.parametrize("fn", ["nb_rmsnorm"])
+def test_norm_arg_checks(fn):
+    lib = L.lib()
+    rc, msg = _err(lib.nb_rmsnorm(16, 100, 16, 16, 128, 4, 128, 1e-6, L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
+    assert lib.nb_rmsnorm(16, 128, 16, 16, 128, 0, 128, 1e-6, L.NB_DTYPE_BF16, None) == 0
