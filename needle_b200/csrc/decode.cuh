@@ -1,9 +1,9 @@
 // Paged split-K decode attention and its merge kernel.
 //
 // Tensor-core path (bf16/fp16, block_size 16, head_dim 64/128, group <= 8):
-//   * one CTA of 4 warps per (split, kv head, sequence); a split is a run of
+//   * one CTA of WARPS warps per (split, kv head, sequence); a split is a run of
 //     `pps` consecutive pages (KV blocks) of the sequence;
-//   * warp w owns pages w, w+4, w+8, ... of its split and runs its own
+//   * warp w owns pages w, w+WARPS, ... of its split and runs its own
 //     STAGES-deep TMA pipeline: each 16-token page of K and of V lands in a
 //     private shared-memory slot (128-byte swizzled, 2 KB per 64 columns),
 //     signalled by a per-slot mbarrier.  Warps never wait on each other
@@ -13,7 +13,7 @@
 //     memory once for all of them), an online softmax with warp shuffles
 //     across the 8 lanes that share a head, P^T re-laid out in registers
 //     with movmatrix, and O^T[D x 8] += V_page^T . P^T on mma again;
-//   * the 4 warps' (m, l, O) are merged through shared memory; a sequence
+//   * the warps' (m, l, O) are merged through shared memory; a sequence
 //     with one split writes the output directly, otherwise fp32 partials go
 //     to the workspace and decode_merge_kernel combines them.
 // SIMT path (fp32, or shapes the tensor-core path does not take): the same
@@ -29,7 +29,6 @@
 
 namespace nb {
 
-constexpr int kTcWarps = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D> struct TcGeom {
@@ -58,8 +57,8 @@ __device__ __forceinline__ void decode_extent(int ctx, int maxb, int bs, int pps
   if (n_splits < 1) n_splits = 1;
 }
 
-template <typename T, int D, int STAGES>
-__global__ void __launch_bounds__(kTcWarps * 32)
+template <typename T, int D, int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32)
     paged_decode_tc_kernel(const __grid_constant__ CUtensorMap kv_map, const T* __restrict__ q,
                            int64_t q_sb, int64_t q_sh, const int32_t* __restrict__ bt,
                            int64_t bt_stride, int maxb, const int32_t* __restrict__ ctx_lens,
@@ -82,18 +81,18 @@ __global__ void __launch_bounds__(kTcWarps * 32)
   if (split >= n_splits) return;
   const int p0 = split * pps;
   const int p1 = min(p0 + pps, n_pages);
-  const int n_w = max(0, (p1 - p0 - warp + kTcWarps - 1) / kTcWarps);
+  const int n_w = max(0, (p1 - p0 - warp + WARPS - 1) / WARPS);
 
   uint8_t* wbase = smem + warp * STAGES * G::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * STAGES * G::kStageBytes) +
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + WARPS * STAGES * G::kStageBytes) +
                    warp * STAGES;
   const uint32_t wbase_u = smem_u32(wbase);
   const uint32_t bar_u = smem_u32(bars);
 
-  // Block ids of this warp's pages: lane i holds page p0 + warp + 4i.
+  // Block ids of this warp's pages: lane i holds page p0 + warp + WARPS * i.
   int my_row = -16;  // first cache row of the page's K slab (OOB -> zero fill)
   if (lane < n_w) {
-    const int phys = __ldg(bt + (int64_t)b * bt_stride + p0 + warp + kTcWarps * lane);
+    const int phys = __ldg(bt + (int64_t)b * bt_stride + p0 + warp + WARPS * lane);
     if (phys >= 0 && phys < num_blocks) my_row = (phys * kvh + h) * 16;
     else set_error(kErrBlockId);
   }
@@ -155,14 +154,19 @@ __global__ void __launch_bounds__(kTcWarps * 32)
     const uint32_t vb = kb + G::kPageBytes;
 
     // S^T = K . Q^T  (16 tokens x 8 heads)
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    // two independent accumulation chains halve the MMA dependency depth
+    float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int kk = 0; kk < NK; ++kk) {
-      uint32_t a[4];
+    for (int kk = 0; kk < NK; kk += 2) {
+      uint32_t a[4], a2[4];
       ldmatrix_x4(a, swz_addr(kb, (lane & 7) + ((mi & 1) << 3), kk * 2 + (mi >> 1)));
+      ldmatrix_x4(a2, swz_addr(kb, (lane & 7) + ((mi & 1) << 3), kk * 2 + 2 + (mi >> 1)));
       Mma<T>::run(sc, a, qf[kk][0], qf[kk][1]);
+      Mma<T>::run(sd, a2, qf[kk + 1][0], qf[kk + 1][1]);
     }
-    const int tok = (p0 + warp + kTcWarps * i) * 16 + g;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sc[e] += sd[e];
+    const int tok = (p0 + warp + WARPS * i) * 16 + g;
     const float x0 = tok < n_tok ? sc[0] * scale_log2 : -INFINITY;
     const float x1 = tok < n_tok ? sc[1] * scale_log2 : -INFINITY;
     const float x2 = tok + 8 < n_tok ? sc[2] * scale_log2 : -INFINITY;
@@ -220,11 +224,16 @@ __global__ void __launch_bounds__(kTcWarps * 32)
     l1 += __shfl_xor_sync(0xffffffffu, l1, sh);
   }
 
-  // In-CTA merge of the 4 warps through shared memory (pipeline slots reused).
+  // Let the merge kernel (launched with programmatic stream serialisation)
+  // get scheduled while this grid drains; it waits for our completion before
+  // reading any partial.
+  griddep_launch_dependents();
+
+  // In-CTA merge of the warps through shared memory (pipeline slots reused).
   __syncthreads();
   float* sm_o = reinterpret_cast<float*>(smem);            // [warps][8][D]
-  float* sm_m = sm_o + kTcWarps * 8 * D;                    // [warps][8]
-  float* sm_l = sm_m + kTcWarps * 8;
+  float* sm_m = sm_o + WARPS * 8 * D;                    // [warps][8]
+  float* sm_l = sm_m + WARPS * 8;
 #pragma unroll
   for (int mt = 0; mt < NK; ++mt) {
     const int d = mt * 16 + g;
@@ -241,14 +250,14 @@ __global__ void __launch_bounds__(kTcWarps * 32)
   }
   __syncthreads();
   const int H = kvh * group;
-  for (int idx = threadIdx.x; idx < group * D; idx += kTcWarps * 32) {
+  for (int idx = threadIdx.x; idx < group * D; idx += WARPS * 32) {
     const int n = idx / D, d = idx - n * D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, sm_m[w * 8 + n]);
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, sm_m[w * 8 + n]);
     float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int w = 0; w < kTcWarps; ++w) {
+    for (int w = 0; w < WARPS; ++w) {
       const float mw = sm_m[w * 8 + n];
       const float e = mw == -INFINITY ? 0.f : exp2f(mw - M);
       L += sm_l[w * 8 + n] * e;
@@ -374,13 +383,19 @@ __global__ void __launch_bounds__(128)
 }
 
 // Combine the split partials of every (sequence, query head) that has more
-// than one split.  One warp per (sequence, head).
+// than one split.  One warp per (sequence, head): lane s reads split s's
+// (m, l), the warp reduces max and normaliser with shuffles, then every lane
+// accumulates its D/32 columns over the splits (independent loads, one
+// memory round trip).  Launched with programmatic stream serialisation: the
+// griddepcontrol.wait below returns once the split kernel has completed and
+// its partials are visible.
 template <typename T>
 __global__ void __launch_bounds__(128)
     decode_merge_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
                         const int32_t* __restrict__ ctx_lens, int maxb, int bs, int pps, int B,
                         int H, int D, int max_splits, T* __restrict__ out, int64_t o_sb,
                         int64_t o_sh) {
+  griddep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pair = blockIdx.x * 4 + warp;
   if (pair >= B * H) return;
@@ -390,21 +405,42 @@ __global__ void __launch_bounds__(128)
   if (n_splits <= 1) return;
   const int64_t base = (int64_t)pair * max_splits;
   float M = -INFINITY;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[base + s].x);
+  for (int s0 = 0; s0 < n_splits; s0 += 32) {
+    const int s = s0 + lane;
+    if (s < n_splits) M = fmaxf(M, part_ml[base + s].x);
+  }
+  M = warp_max(M);
   float L = 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float2 ml = part_ml[base + s];
-    L += ml.y * (ml.x == -INFINITY ? 0.f : exp2f(ml.x - M));
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int d = lane; d < D; d += 32) {
-    float O = 0.f;
-    for (int s = 0; s < n_splits; ++s) {
-      const float mx = part_ml[base + s].x;
-      O += part_o[(base + s) * D + d] * (mx == -INFINITY ? 0.f : exp2f(mx - M));
+  for (int s0 = 0; s0 < n_splits; s0 += 32) {
+    const int s = s0 + lane;
+    if (s < n_splits) {
+      const float2 ml = part_ml[base + s];
+      L += ml.y * (ml.x == -INFINITY ? 0.f : exp2f(ml.x - M));
     }
-    out[(int64_t)b * o_sb + (int64_t)qh * o_sh + d] = Dt<T>::from_f(O * inv);
   }
+  L = warp_sum(L);
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int epl = D / 32;  // columns per lane (D is a multiple of 32)
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int s0 = 0; s0 < n_splits; s0 += 32) {
+    const int sl = s0 + lane;
+    const float2 ml = sl < n_splits ? part_ml[base + sl] : make_float2(-INFINITY, 0.f);
+    const float wl = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+    const int cnt = min(32, n_splits - s0);
+    for (int j = 0; j < cnt; ++j) {
+      const float w = __shfl_sync(0xffffffffu, wl, j);
+      const float* src = part_o + (base + s0 + j) * D + lane * epl;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < epl) acc[e] = fmaf(src[e], w, acc[e]);
+    }
+  }
+  T* dst = out + (int64_t)b * o_sb + (int64_t)qh * o_sh + lane * epl;
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    if (e < epl) dst[e] = Dt<T>::from_f(acc[e] * inv);
 }
 
 }  // namespace nb
@@ -414,20 +450,37 @@ __global__ void __launch_bounds__(128)
 // ---------------------------------------------------------------------------
 namespace nbh {
 
-constexpr int kMaxPagesPerSplitTc = 32 * nb::kTcWarps;  // one page id per lane per warp
+// Tensor-core decode configuration: warps per CTA and TMA pipeline depth per
+// warp.  Each warp keeps one page id per lane, so a split holds at most
+// 32 * warps pages.
+struct TcCfg {
+  int warps, stages;
+};
 
-inline int decode_stages() { return 4; }
+inline TcCfg decode_cfg() {
+  static TcCfg cfg = [] {
+    TcCfg c{4, 2};
+    if (const char* e = getenv("NB_DECODE_CFG")) {  // tuning knob: "warps,stages"
+      int w = 0, s = 0;
+      if (sscanf(e, "%d,%d", &w, &s) == 2 &&
+          ((w == 4 && (s == 2 || s == 3 || s == 4)) || (w == 8 && s == 2)))
+        c = TcCfg{w, s};
+    }
+    return c;
+  }();
+  return cfg;
+}
 
-template <typename T, int D, int STAGES>
+template <typename T, int D, int WARPS, int STAGES>
 int launch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t qsh,
                      const int32_t* bt, int64_t bts, int maxb, const int32_t* ctx, int kvh,
                      int group, int nblk, float scale_log2, int pps, void* out, int64_t osb,
                      int64_t osh, float* po, float2* pml, int max_splits, int B, cudaStream_t st) {
   using G = nb::TcGeom<D>;
-  const size_t smem = 1024 + (size_t)nb::kTcWarps * STAGES * G::kStageBytes +
-                      (size_t)nb::kTcWarps * STAGES * 8;
+  const size_t smem =
+      1024 + (size_t)WARPS * STAGES * G::kStageBytes + (size_t)WARPS * STAGES * 8;
   static bool attr_set = false;
-  auto kern = nb::paged_decode_tc_kernel<T, D, STAGES>;
+  auto kern = nb::paged_decode_tc_kernel<T, D, WARPS, STAGES>;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
@@ -435,10 +488,28 @@ int launch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t
     attr_set = true;
   }
   dim3 grid(max_splits, kvh, B);
-  kern<<<grid, nb::kTcWarps * 32, smem, st>>>(map, (const T*)q, qsb, qsh, bt, bts, maxb, ctx, kvh,
-                                              group, nblk, scale_log2, pps, (T*)out, osb, osh, po,
-                                              pml, max_splits);
+  kern<<<grid, WARPS * 32, smem, st>>>(map, (const T*)q, qsb, qsh, bt, bts, maxb, ctx, kvh, group,
+                                       nblk, scale_log2, pps, (T*)out, osb, osh, po, pml,
+                                       max_splits);
   return check_launch("paged_decode_tc");
+}
+
+template <typename T, int D>
+int dispatch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t qsh,
+                       const int32_t* bt, int64_t bts, int maxb, const int32_t* ctx, int kvh,
+                       int group, int nblk, float sl2, int pps, void* out, int64_t osb,
+                       int64_t osh, float* po, float2* pml, int ms, int B, cudaStream_t st) {
+  const TcCfg c = decode_cfg();
+#define NB_TC(W, S)                                                                           \
+  if (c.warps == W && c.stages == S)                                                          \
+    return launch_decode_tc<T, D, W, S>(map, q, qsb, qsh, bt, bts, maxb, ctx, kvh, group,     \
+                                        nblk, sl2, pps, out, osb, osh, po, pml, ms, B, st);
+  NB_TC(4, 3)
+  NB_TC(4, 4)
+  NB_TC(8, 2)
+#undef NB_TC
+  return launch_decode_tc<T, D, 4, 2>(map, q, qsb, qsh, bt, bts, maxb, ctx, kvh, group, nblk, sl2,
+                                      pps, out, osb, osh, po, pml, ms, B, st);
 }
 
 template <typename T, int D>
@@ -485,10 +556,23 @@ int launch_merge(const float* po, const float2* pml, const int32_t* ctx, int max
                  int B, int H, int D, int max_splits, void* out, int64_t osb, int64_t osh,
                  cudaStream_t st) {
   const int pairs = B * H;
-  nb::decode_merge_kernel<T><<<(pairs + 3) / 4, 128, 0, st>>>(
-      po, pml, ctx, maxb, bs, pps, B, H, D, max_splits, (T*)out, osb, osh);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((pairs + 3) / 4);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, nb::decode_merge_kernel<T>, po, pml, ctx, maxb, bs,
+                                     pps, B, H, D, max_splits, (T*)out, osb, osh);
+  if (e != cudaSuccess) return fail(NB_ERR_CUDA, "decode_merge launch: %s", cudaGetErrorString(e));
   return check_launch("decode_merge");
 }
+
+inline int max_pages_per_split_tc() { return 32 * decode_cfg().warps; }
 
 }  // namespace nbh
 
@@ -509,7 +593,7 @@ int nb_paged_decode_plan(int num_seqs, int num_kv_heads, int max_blocks_per_seq,
   pps = (pps + 3) / 4 * 4;
   const int lo = 8 * 16 / block_size > 0 ? 8 * 16 / block_size : 1;  // >= 128 tokens per split
   if (pps < lo) pps = lo;
-  if (pps > kMaxPagesPerSplitTc) pps = kMaxPagesPerSplitTc;
+  if (pps > 128) pps = 128;
   if (pps > max_blocks_per_seq) pps = max_blocks_per_seq;
   *pages_per_split = pps;
   *max_splits = (max_blocks_per_seq + pps - 1) / pps;
@@ -543,6 +627,7 @@ int nb_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
   if (block_table_stride < max_blocks_per_seq)
     return fail(NB_ERR_INVALID_ARG, "block_table_stride < max_blocks_per_seq");
   if (pages_per_split <= 0) return fail(NB_ERR_INVALID_ARG, "pages_per_split must be > 0");
+  if (head_dim % 32) return fail(NB_ERR_UNSUPPORTED, "head_dim must be a multiple of 32");
   if (q_stride_head < head_dim || out_stride_head < head_dim ||
       q_stride_seq < (int64_t)num_q_heads * q_stride_head - (q_stride_head - head_dim) ||
       out_stride_seq < (int64_t)num_q_heads * out_stride_head - (out_stride_head - head_dim))
@@ -564,7 +649,7 @@ int nb_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
   const int64_t rows = 2ll * num_blocks * num_kv_heads * block_size;
   const bool tc = dtype != NB_DTYPE_F32 && block_size == 16 &&
                   (head_dim == 64 || head_dim == 128) && group <= 8 &&
-                  pages_per_split <= kMaxPagesPerSplitTc && rows < (1ll << 31) &&
+                  pages_per_split <= max_pages_per_split_tc() && rows < (1ll << 31) &&
                   (uintptr_t)kv_cache % 16 == 0 && (uintptr_t)q % 4 == 0 &&
                   q_stride_seq % 2 == 0 && q_stride_head % 2 == 0;
   int rc;
@@ -572,36 +657,38 @@ int nb_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
     CUtensorMap map;
     rc = tensor_map_2d(&map, kv_cache, dtype, head_dim, rows, (uint64_t)head_dim * 2, 64, 16);
     if (rc) return rc;
-    if (dtype == NB_DTYPE_BF16) {
-      rc = head_dim == 64
-               ? launch_decode_tc<__nv_bfloat16, 64, 4>(map, q, q_stride_seq, q_stride_head, block_table, block_table_stride, max_blocks_per_seq, context_lens, num_kv_heads, group, num_blocks, sl2, pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits, num_seqs, st)
-               : launch_decode_tc<__nv_bfloat16, 128, 4>(map, q, q_stride_seq, q_stride_head, block_table, block_table_stride, max_blocks_per_seq, context_lens, num_kv_heads, group, num_blocks, sl2, pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits, num_seqs, st);
-    } else {
-      rc = head_dim == 64
-               ? launch_decode_tc<__half, 64, 4>(map, q, q_stride_seq, q_stride_head, block_table, block_table_stride, max_blocks_per_seq, context_lens, num_kv_heads, group, num_blocks, sl2, pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits, num_seqs, st)
-               : launch_decode_tc<__half, 128, 4>(map, q, q_stride_seq, q_stride_head, block_table, block_table_stride, max_blocks_per_seq, context_lens, num_kv_heads, group, num_blocks, sl2, pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits, num_seqs, st);
-    }
+#define NB_ARGS map, q, q_stride_seq, q_stride_head, block_table, block_table_stride,           \
+                max_blocks_per_seq, context_lens, num_kv_heads, group, num_blocks, sl2,         \
+                pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits,     \
+                num_seqs, st
+    if (dtype == NB_DTYPE_BF16)
+      rc = head_dim == 64 ? dispatch_decode_tc<__nv_bfloat16, 64>(NB_ARGS)
+                          : dispatch_decode_tc<__nv_bfloat16, 128>(NB_ARGS);
+    else
+      rc = head_dim == 64 ? dispatch_decode_tc<__half, 64>(NB_ARGS)
+                          : dispatch_decode_tc<__half, 128>(NB_ARGS);
+#undef NB_ARGS
   } else {
+#define NB_ARGS head_dim, kv_cache, num_blocks, num_kv_heads, block_size, q, q_stride_seq,      \
+                q_stride_head, block_table, block_table_stride, max_blocks_per_seq,             \
+                context_lens, group, sl2, pages_per_split, out, out_stride_seq,                 \
+                out_stride_head, po, pml, max_splits, num_seqs, st
     switch (dtype) {
-      case NB_DTYPE_F32:
-        rc = launch_decode_simt_d<float>(head_dim, kv_cache, num_blocks, num_kv_heads, block_size, q, q_stride_seq, q_stride_head, block_table, block_table_stride, max_blocks_per_seq, context_lens, group, sl2, pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits, num_seqs, st);
-        break;
-      case NB_DTYPE_F16:
-        rc = launch_decode_simt_d<__half>(head_dim, kv_cache, num_blocks, num_kv_heads, block_size, q, q_stride_seq, q_stride_head, block_table, block_table_stride, max_blocks_per_seq, context_lens, group, sl2, pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits, num_seqs, st);
-        break;
-      default:
-        rc = launch_decode_simt_d<__nv_bfloat16>(head_dim, kv_cache, num_blocks, num_kv_heads, block_size, q, q_stride_seq, q_stride_head, block_table, block_table_stride, max_blocks_per_seq, context_lens, group, sl2, pages_per_split, out, out_stride_seq, out_stride_head, po, pml, max_splits, num_seqs, st);
+      case NB_DTYPE_F32: rc = launch_decode_simt_d<float>(NB_ARGS); break;
+      case NB_DTYPE_F16: rc = launch_decode_simt_d<__half>(NB_ARGS); break;
+      default: rc = launch_decode_simt_d<__nv_bfloat16>(NB_ARGS);
     }
+#undef NB_ARGS
   }
   if (rc || max_splits <= 1) return rc;
+#define NB_ARGS po, pml, context_lens, max_blocks_per_seq, block_size, pages_per_split, num_seqs, \
+                num_q_heads, head_dim, max_splits, out, out_stride_seq, out_stride_head, st
   switch (dtype) {
-    case NB_DTYPE_F32:
-      return launch_merge<float>(po, pml, context_lens, max_blocks_per_seq, block_size, pages_per_split, num_seqs, num_q_heads, head_dim, max_splits, out, out_stride_seq, out_stride_head, st);
-    case NB_DTYPE_F16:
-      return launch_merge<__half>(po, pml, context_lens, max_blocks_per_seq, block_size, pages_per_split, num_seqs, num_q_heads, head_dim, max_splits, out, out_stride_seq, out_stride_head, st);
-    default:
-      return launch_merge<__nv_bfloat16>(po, pml, context_lens, max_blocks_per_seq, block_size, pages_per_split, num_seqs, num_q_heads, head_dim, max_splits, out, out_stride_seq, out_stride_head, st);
+    case NB_DTYPE_F32: return launch_merge<float>(NB_ARGS);
+    case NB_DTYPE_F16: return launch_merge<__half>(NB_ARGS);
+    default: return launch_merge<__nv_bfloat16>(NB_ARGS);
   }
+#undef NB_ARGS
 }
 
 }  // extern "C"

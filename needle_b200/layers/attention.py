@@ -1,0 +1,66 @@
+"""Drop-in replacement for needle's ``Attention`` module on the B200 kernels.
+
+Same constructor (``needle/layers/attention.py:36-63``), same parameter names
+(``q_proj``/``k_proj``/``v_proj``/``o_proj``, so needle state dicts load
+unchanged) and the same ``forward`` signature and contract
+(``needle/layers/attention.py:70-96``):
+
+    forward(hidden_states [T, hidden], positions [T], kv_cache [2, N, kv, bs, D],
+            block_table [B, maxb] int32, cu_seqlens [B+1] int32,
+            context_lens [B] int32, max_seqlen, is_prefill, cos [T, D], sin [T, D])
+        -> [T, hidden]
+
+What changes is underneath: RoPE and the KV-cache write are one fused kernel
+(``rope_store_kvcache``); prefill attention and paged split-K decode are
+hand-written sm_100a kernels; none of needle's per-layer host syncs
+(``.cpu()`` at attention.py:111,170,222-223,297) or Python loops over
+sequences remain.  The KV cache is mutated in place, as in needle.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from .linear import ColumnParallelLinear, RowParallelLinear
+
+
+class Attention(nn.Module):
+    def __init__(self, config, layer_idx: int, tp_size: int = 1, tp_rank: int = 0,
+                 qkv_bias: bool = False):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.num_heads = config.num_attention_heads // tp_size
+        self.num_kv_heads = max(1, config.num_key_value_heads // tp_size)
+        self.head_dim = config.head_dim
+        self.scale = 1.0 / math.sqrt(self.head_dim)
+        H, KV, D = config.num_attention_heads, config.num_key_value_heads, config.head_dim
+        self.q_proj = ColumnParallelLinear(config.hidden_size, H * D, bias=qkv_bias,
+                                           tp_size=tp_size, tp_rank=tp_rank)
+        self.k_proj = ColumnParallelLinear(config.hidden_size, KV * D, bias=qkv_bias,
+                                           tp_size=tp_size, tp_rank=tp_rank)
+        self.v_proj = ColumnParallelLinear(config.hidden_size, KV * D, bias=qkv_bias,
+                                           tp_size=tp_size, tp_rank=tp_rank)
+        self.o_proj = RowParallelLinear(H * D, config.hidden_size, tp_size=tp_size,
+                                        tp_rank=tp_rank)
+
+    def forward(self, hidden_states, positions, kv_cache, block_table, cu_seqlens,
+                context_lens, max_seqlen, is_prefill, cos, sin):
+        T = hidden_states.shape[0]
+        H, KV, D = self.num_heads, self.num_kv_heads, self.head_dim
+        q = self.q_proj(hidden_states).view(T, H, D)
+        k = self.k_proj(hidden_states).view(T, KV, D)
+        v = self.v_proj(hidden_states).view(T, KV, D)
+        if is_prefill:
+            ops.rope_store_kvcache(q, k, v, cos, sin, kv_cache, block_table, context_lens,
+                                   cu_seqlens=cu_seqlens, write_k_back=True)
+            attn = ops.prefill_attention(q, k, v, cu_seqlens, max_seqlen, self.scale)
+        else:
+            ops.rope_store_kvcache(q, k, v, cos, sin, kv_cache, block_table, context_lens)
+            plan = ops.decode_plan(T, H, KV, D, block_table.shape[1], kv_cache.shape[3],
+                                   q.device)
+            attn = ops.paged_decode(q, kv_cache, block_table, context_lens, self.scale,
+                                    plan=plan)
+        return self.o_proj(attn.view(T, H * D))

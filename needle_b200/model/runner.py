@@ -1,0 +1,233 @@
+"""ModelRunner with needle's API on the B200 attention path.
+
+Mirrors ``needle/model/runner.py:14-249``: the same constructor arguments,
+``profile_memory``, ``init_kv_cache`` (per-layer caches of shape
+``[2, num_blocks, num_kv_heads, block_size, head_dim]``), ``execute
+(SchedulerOutput) -> ExecuteOutput`` (mixed prefill/decode batches run as two
+forwards, ``:121-153``), ``_prepare_inputs`` (the same ``input_ids``,
+``positions``, ``cu_seqlens``, ``context_lens`` and dummy-padded
+``block_table``, ``:194-249``) and block swapping (``:175-192``).  It works
+with needle's own Scheduler / BlockAllocator / SchedulerOutput objects or
+with the mirrors in ``needle_b200.model.sequence``.
+
+Differences, all below the API: the model is materialised directly on the
+device (no CPU copy of the weights); host-built step inputs are copied from
+pinned memory without a blocking sync; greedy sampling is one batched
+argmax with a single device-to-host read (needle reads one ``int(argmax)``
+per sequence, ``needle/model/sampler.py:27-28``).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn.functional as F
+
+from ..layers.linear import shard_for_rank
+from ..layers.rope import RotaryEmbedding
+from .config import ModelConfig
+from .llama import LlamaForCausalLM
+from .qwen2 import Qwen2ForCausalLM
+from .sequence import ExecuteInput, ExecuteOutput, SchedulerOutput
+
+
+def build_model(config: ModelConfig, tp_size: int = 1, tp_rank: int = 0):
+    """``needle/model/__init__.py:8-17``: pick the class from ``model_type``."""
+    mt = config.model_type.lower()
+    if mt == "llama":
+        return LlamaForCausalLM(config, tp_size=tp_size, tp_rank=tp_rank)
+    if mt == "qwen2":
+        return Qwen2ForCausalLM(config, tp_size=tp_size, tp_rank=tp_rank)
+    raise ValueError(f"Unsupported model_type: {mt!r}")
+
+
+class Sampler:
+    """Top-k / top-p / temperature sampling (``needle/model/sampler.py:13-48``).
+
+    Rows with temperature 0 take one batched argmax and one host read; other
+    rows follow needle's per-row recipe.
+    """
+
+    @torch.no_grad()
+    def sample(self, logits: torch.Tensor, params_list) -> List[int]:
+        assert logits.shape[0] == len(params_list)
+        greedy = [p.temperature == 0.0 for p in params_list]
+        out: List[Optional[int]] = [None] * len(params_list)
+        if any(greedy):
+            ids = logits.argmax(dim=-1).tolist()
+            for i, g in enumerate(greedy):
+                if g:
+                    out[i] = ids[i]
+        for i, p in enumerate(params_list):
+            if greedy[i]:
+                continue
+            logit = logits[i] / p.temperature
+            if p.top_k > 0:
+                k = min(p.top_k, logit.size(-1))
+                kth = logit.topk(k).values[-1]
+                logit = logit.masked_fill(logit < kth, float("-inf"))
+            if p.top_p < 1.0:
+                sl, si = logit.sort(descending=True)
+                probs = sl.softmax(dim=-1)
+                remove = probs.cumsum(dim=-1) - probs > p.top_p
+                sl[remove] = float("-inf")
+                logit = logit.scatter(0, si, sl)
+            out[i] = int(torch.multinomial(F.softmax(logit, dim=-1), num_samples=1))
+        return out  # type: ignore[return-value]
+
+
+class ModelRunner:
+    def __init__(self, model_config: ModelConfig, block_size: int = 16, dtype: str = "bfloat16",
+                 device: str = "cuda", tensor_parallel_size: int = 1, tp_rank: int = 0):
+        self.model_config = model_config
+        self.block_size = block_size
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("needle_b200 runs on CUDA devices only")
+        self.tp_size = tensor_parallel_size
+        self.tp_rank = tp_rank
+        self.dtype = getattr(torch, dtype) if isinstance(dtype, str) else dtype
+        with torch.device("meta"):
+            model = build_model(model_config, tp_size=tensor_parallel_size, tp_rank=tp_rank)
+        model = model.to_empty(device=self.device).to(self.dtype)
+        cfg = model_config
+        # RoPE tables are computed on the CPU exactly as needle computes them,
+        # then moved and cast like the rest of the model.
+        model.model.rotary_emb = RotaryEmbedding(
+            cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta).to(self.device, self.dtype)
+        model.eval()
+        self.model = model
+        self.sampler = Sampler()
+        self.kv_caches: List[torch.Tensor] = []
+        self.cpu_kv_caches: List[torch.Tensor] = []
+
+    # ------------------------------------------------------------------ weights
+
+    @torch.no_grad()
+    def load_state_dict(self, state_dict: Dict[str, torch.Tensor]) -> None:
+        """Load a full (unsharded) needle-named state dict, sharding for this
+        rank like ``needle/model/loader.py:100-149`` (lm_head tied to the
+        embedding when absent)."""
+        params = dict(self.model.named_parameters())
+        missing = set(params)
+        for name, p in params.items():
+            src = state_dict.get(name)
+            if src is None and name == "lm_head.weight":
+                src = state_dict.get("model.embed_tokens.weight")
+            if src is None:
+                continue
+            t = shard_for_rank(name, src, self.tp_size, self.tp_rank)
+            if tuple(t.shape) != tuple(p.shape):
+                raise ValueError(f"Shape mismatch for {name}: {tuple(t.shape)} vs {tuple(p.shape)}")
+            p.copy_(t.to(device=p.device, dtype=p.dtype))
+            missing.discard(name)
+        if missing:
+            raise ValueError(f"missing weights: {sorted(missing)[:8]}")
+
+    @torch.no_grad()
+    def init_synthetic(self, seed: int = 0) -> None:
+        """Fill every parameter with the synthetic distributions of
+        ``needle_b200.synth`` generated on the device (for large benchmark
+        models; values differ from the CPU-generated ones)."""
+        from ..synth import synth_tensor, weight_shapes
+        params = dict(self.model.named_parameters())
+        for name, shape, kind in weight_shapes(self.model_config):
+            full = synth_tensor(name, shape, kind, seed=seed, device=self.device,
+                                dtype=torch.float32)
+            params[name].copy_(shard_for_rank(name, full, self.tp_size, self.tp_rank))
+            del full
+        if self.model_config.tie_word_embeddings:
+            params["lm_head.weight"].copy_(params["model.embed_tokens.weight"])
+
+    # ------------------------------------------------------------------ memory
+
+    def kv_bytes_per_block(self) -> int:
+        cfg = self.model_config
+        kvh = max(1, cfg.num_key_value_heads // self.tp_size)
+        elt = torch.tensor([], dtype=self.dtype).element_size()
+        return 2 * kvh * self.block_size * cfg.head_dim * elt * cfg.num_hidden_layers
+
+    def profile_memory(self, gpu_memory_utilization: float = 0.90):
+        """Blocks that fit in the free device memory (``runner.py:44-63``)."""
+        free, _total = torch.cuda.mem_get_info(self.device)
+        n = max(1, int(free * gpu_memory_utilization) // self.kv_bytes_per_block())
+        return n, n // 2
+
+    def init_kv_cache(self, num_gpu_blocks: int, num_cpu_blocks: int) -> None:
+        cfg = self.model_config
+        kvh = max(1, cfg.num_key_value_heads // self.tp_size)
+        shape = (2, num_gpu_blocks, kvh, self.block_size, cfg.head_dim)
+        self.kv_caches = [torch.zeros(shape, dtype=self.dtype, device=self.device)
+                          for _ in range(cfg.num_hidden_layers)]
+        self.cpu_kv_caches = []
+        if num_cpu_blocks > 0:
+            cshape = (2, num_cpu_blocks, kvh, self.block_size, cfg.head_dim)
+            self.cpu_kv_caches = [torch.zeros(cshape, dtype=self.dtype, pin_memory=True)
+                                  for _ in range(cfg.num_hidden_layers)]
+
+    # ------------------------------------------------------------------ step
+
+    def execute(self, sched_out) -> ExecuteOutput:
+        if sched_out.swap_out_map and self.cpu_kv_caches:
+            self._swap_kv_blocks(sched_out.swap_out_map, "gpu_to_cpu")
+        if sched_out.swap_in_map and self.cpu_kv_caches:
+            self._swap_kv_blocks(sched_out.swap_in_map, "cpu_to_gpu")
+        all_seqs = list(sched_out.prefill_seqs) + list(sched_out.decode_seqs)
+        with torch.no_grad():
+            if sched_out.prefill_seqs and sched_out.decode_seqs:
+                pre = self._prepare_inputs(sched_out.prefill_seqs, [], sched_out.block_tables)
+                dec = self._prepare_inputs([], sched_out.decode_seqs, sched_out.block_tables)
+                logits = torch.cat([self._forward(pre), self._forward(dec)], dim=0)
+            else:
+                inp = self._prepare_inputs(sched_out.prefill_seqs, sched_out.decode_seqs,
+                                           sched_out.block_tables)
+                logits = self._forward(inp)
+        params = [s.request.sampling_params for s in all_seqs]
+        return ExecuteOutput(seq_ids=[s.seq_id for s in all_seqs],
+                             next_token_ids=self.sampler.sample(logits, params))
+
+    def _forward(self, inp: ExecuteInput) -> torch.Tensor:
+        return self.model(inp.input_ids, inp.position_ids, self.kv_caches, inp.block_table,
+                          inp.cu_seqlens, inp.context_lens, inp.max_seqlen, inp.is_prefill)
+
+    def _swap_kv_blocks(self, mapping: dict, direction: str) -> None:
+        """Copy whole blocks between the device and pinned host caches
+        (``needle/model/runner.py:175-192``), one gathered copy per layer."""
+        src = torch.tensor(list(mapping.keys()), dtype=torch.long)
+        dst = torch.tensor(list(mapping.values()), dtype=torch.long)
+        for gpu, cpu in zip(self.kv_caches, self.cpu_kv_caches):
+            if direction == "gpu_to_cpu":
+                cpu[:, dst] = gpu[:, src.to(self.device)].cpu()
+            else:
+                gpu[:, dst.to(self.device)] = cpu[:, src].to(self.device, non_blocking=True)
+
+    def _h2d(self, data, dtype) -> torch.Tensor:
+        return torch.tensor(data, dtype=dtype).pin_memory().to(self.device, non_blocking=True)
+
+    def _prepare_inputs(self, prefill_seqs, decode_seqs, block_tables) -> ExecuteInput:
+        all_seqs = list(prefill_seqs) + list(decode_seqs)
+        is_prefill = len(decode_seqs) == 0 or len(prefill_seqs) > 0
+        ids: List[int] = []
+        pos: List[int] = []
+        cu: List[int] = [0]
+        ctx: List[int] = []
+        for seq in all_seqs:
+            if seq.num_generated_tokens == 0:
+                toks, c = seq.token_ids, 0
+            else:
+                toks, c = [seq.last_token_id], seq.length - 1
+            ids.extend(toks)
+            pos.extend(range(c, c + len(toks)))
+            cu.append(cu[-1] + len(toks))
+            ctx.append(c)
+        maxb = max((len(block_tables.get(s.seq_id, [])) for s in all_seqs), default=1)
+        maxb = max(maxb, 1)
+        dummy = (self.kv_caches[0].shape[1] if self.kv_caches else 1) - 1
+        bt = [block_tables.get(s.seq_id, []) + [dummy] * (maxb - len(block_tables.get(s.seq_id, [])))
+              for s in all_seqs]
+        max_seqlen = max((cu[i + 1] - cu[i] for i in range(len(all_seqs))), default=1)
+        return ExecuteInput(input_ids=self._h2d(ids, torch.long),
+                            position_ids=self._h2d(pos, torch.long),
+                            cu_seqlens=self._h2d(cu, torch.int32), max_seqlen=max_seqlen,
+                            block_table=self._h2d(bt, torch.int32),
+                            context_lens=self._h2d(ctx, torch.int32), is_prefill=is_prefill)

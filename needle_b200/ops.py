@@ -165,6 +165,23 @@ class DecodePlan:
         self.key = (num_seqs, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size)
 
 
+_PLANS: "dict" = {}
+
+
+def decode_plan(num_seqs: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                max_blocks: int, block_size: int, device) -> DecodePlan:
+    """A cached ``DecodePlan`` for this shape: every layer of a decode step (and
+    every step with the same batch shape) shares one plan and workspace."""
+    key = (num_seqs, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, str(device))
+    p = _PLANS.get(key)
+    if p is None:
+        if len(_PLANS) > 64:
+            _PLANS.clear()
+        p = _PLANS[key] = DecodePlan(num_seqs, num_q_heads, num_kv_heads, head_dim, max_blocks,
+                                     block_size, device)
+    return p
+
+
 def paged_decode(q: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
                  context_lens: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
                  plan: Optional[DecodePlan] = None) -> torch.Tensor:
