@@ -1,10 +1,11 @@
-// Causal prefill attention over each sequence's new tokens (SIMT path).
+// Causal prefill attention over each sequence's new tokens.
 //
-// One warp per (query token, query head); a CTA holds 4 consecutive queries
-// of one head, so they stream the same keys through L1.  Online softmax in
-// base 2 with shuffle-reduced dot products.  This path is exact enough for
-// the fp32 configurations and is the fallback for shapes the tensor-core
-// prefill does not take.
+// prefill_tc_kernel (below) is the bf16/fp16 path on the 5th-generation
+// tensor cores.  prefill_simt_kernel is the fp32 path and the fallback for
+// head dims the tensor-core kernel does not take: one warp per (query token,
+// query head), a CTA holds 4 consecutive queries of one head so they stream
+// the same keys through L1, online softmax in base 2 with shuffle-reduced dot
+// products.
 #pragma once
 #include "nb_common.cuh"
 
@@ -53,6 +54,245 @@ __global__ void __launch_bounds__(128)
     out[(int64_t)tq * os + (int64_t)head * D + lane * EPL + e] = Dt<T>::from_f(acc[e] * inv);
 }
 
+
+// ---------------------------------------------------------------------------
+// Tensor-core prefill (bf16/fp16, head_dim 64/128) on tcgen05 + TMEM.
+//
+// One CTA of 4 warps per (128-query tile, query head, sequence).  Q, K and V
+// tiles (128 rows x 64 columns per 16 KB atom, 128-byte swizzle) arrive by
+// TMA; K/V are double-buffered.  Per KV tile j (causal: j = 0..tile):
+//   S[128 x 128] = Q . K_j^T        tcgen05.mma into TMEM columns [0, 128)
+//   each thread owns one query row (= one TMEM lane): pass 1 over its S row
+//   finds the tile max, pass 2 writes P = exp2(s - m) (bf16/fp16, swizzled)
+//   to shared memory and sums it
+//   O += P . V_j                    tcgen05.mma into TMEM columns [128, 128+D)
+// O stays in TMEM for the whole row of tiles.  The running max m is only
+// raised when a tile's max exceeds it by more than 8 (log2 units, a factor of
+// 256); then the warp rescales its O rows in TMEM (ld, multiply, st).  With a
+// stale m every p is at most 2^8, far inside fp32/bf16 range, and O / l is
+// exact, so the lazy update changes no result but skips almost all
+// rescaling.  The P.V MMA of tile j runs while the S MMA and the max pass of
+// tile j+1 proceed.  One thread issues the MMAs and TMA loads and commits the
+// MMAs to mbarriers; every wait is bounded.
+// ---------------------------------------------------------------------------
+template <int D> struct PfGeom {
+  static constexpr int kAtom = 128 * 128;            // 128 rows x 128 B
+  static constexpr int kTile = (D / 64) * kAtom;     // one Q, K or V tile
+  static constexpr int kQ = 0;
+  static constexpr int kK = kTile;                   // 2 stages
+  static constexpr int kV = kK + 2 * kTile;          // 2 stages
+  static constexpr int kP = kV + 2 * kTile;          // 128 x 128 probabilities
+  static constexpr int kBars = kP + 2 * kAtom;
+  static constexpr int kSmem = kBars + 64 + 1024;
+  static constexpr uint32_t kTmemCols = 256;         // S: 128 columns, O: D columns
+};
+
+constexpr float kRescaleThreshold = 8.0f;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                      const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
+                      int group, float scale_log2, T* __restrict__ out, int64_t os) {
+  using G = PfGeom<D>;
+  constexpr bool kBf16 = !__is_same(T, __half);
+  constexpr uint32_t kIdS = idesc_f16_f32(kBf16, 128, 128, false, false);
+  constexpr uint32_t kIdO = idesc_f16_f32(kBf16, 128, D, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int s0 = __ldg(cu + b), len = __ldg(cu + b + 1) - s0;
+  const int q0 = qt * 128;
+  if (q0 >= len) return;
+  const int kh = h / group;
+  const int n_kv = qt + 1;
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t bar_q = sb + G::kBars, bar_s = bar_q + 8, bar_o = bar_q + 16;
+  const uint32_t bar_kv0 = bar_q + 24;  // + 8 * stage
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kBars + 48);
+
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), G::kTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    mbar_init(bar_q, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_kv0, 1);
+    mbar_init(bar_kv0 + 8, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  auto load_kv = [&](int j) {  // thread 0 only
+    const int st = j & 1;
+    const uint32_t bar = bar_kv0 + 8 * st;
+    mbar_arrive_expect_tx(bar, 2 * G::kTile);
+#pragma unroll
+    for (int a = 0; a < D / 64; ++a) {
+      tma_load_2d(sb + G::kK + st * G::kTile + a * G::kAtom, &kmap, kh * D + a * 64,
+                  s0 + j * 128, bar);
+      tma_load_2d(sb + G::kV + st * G::kTile + a * G::kAtom, &vmap, kh * D + a * 64,
+                  s0 + j * 128, bar);
+    }
+  };
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_q, G::kTile);
+#pragma unroll
+    for (int a = 0; a < D / 64; ++a)
+      tma_load_2d(sb + G::kQ + a * G::kAtom, &qmap, h * D + a * 64, s0 + q0, bar_q);
+    load_kv(0);
+    if (n_kv > 1) load_kv(1);
+  }
+
+  const int r = warp * 32 + lane;  // query row of this thread = TMEM lane
+  const int qi = q0 + r;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  float m = -INFINITY, l = 0.f;
+  bool failed = false;
+
+  for (int j = 0; j < n_kv; ++j) {
+    const int st = j & 1;
+    if (tid == 0) {
+      bool w = j > 0 || mbar_wait_bounded(bar_q, 0);
+      w = w && mbar_wait_bounded(bar_kv0 + 8 * st, (j >> 1) & 1);
+      if (w) {
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
+          tc_mma_f16_ss(tS, smem_desc_sw128(sb + G::kQ + off, 16, 1024),
+                        smem_desc_sw128(sb + G::kK + st * G::kTile + off, 16, 1024), kIdS,
+                        kk > 0);
+        }
+        tc_commit(bar_s);
+      }
+    }
+    if (__syncthreads_or(!mbar_wait_bounded(bar_s, j & 1))) { failed = true; break; }
+    tc_fence_after();
+
+    // pass 1: this tile's row max of the scaled, masked scores
+    const int kb = j * 128;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(tS + lane_off + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int col = kb + c * 32 + i;
+        if (col <= qi && col < len) mx = fmaxf(mx, v[i] * scale_log2);
+      }
+    }
+    // P.V of the previous tile must be done before P is overwritten, O is
+    // rescaled or its V stage is refilled.
+    if (j > 0) {
+      if (__syncthreads_or(!mbar_wait_bounded(bar_o, (j - 1) & 1))) { failed = true; break; }
+      tc_fence_after();
+      if (tid == 0 && j + 1 < n_kv) load_kv(j + 1);
+    }
+    const bool need = mx > m + kRescaleThreshold;  // also true on the first valid tile
+    float alpha = 1.f;
+    if (need) {
+      alpha = exp2f(m - mx);  // 0 when m is still -inf
+      m = mx;
+    }
+    // pass 2: probabilities into the swizzled P tile, row sum
+    float rs = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(tS + lane_off + c * 32, v);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {  // 4 chunks of 8 columns
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i0 = k * 8 + 2 * e;
+          const int col = kb + c * 32 + i0;
+          const float p0 = (col <= qi && col < len) ? exp2f(v[i0] * scale_log2 - m) : 0.f;
+          const float p1 =
+              (col + 1 <= qi && col + 1 < len) ? exp2f(v[i0 + 1] * scale_log2 - m) : 0.f;
+          rs += p0 + p1;
+          pk[e] = Mma<T>::pack(p0, p1);
+        }
+        const int cc = c * 4 + k;  // 16-byte chunk index 0..15 along the 128 columns
+        const uint32_t addr =
+            G::kP + (cc >> 3) * G::kAtom + r * 128 + (((cc & 7) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(smem + addr) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+    l = l * alpha + rs;
+    // rescale this warp's O rows in TMEM when any of its rows raised m
+    if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(tO + lane_off + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= alpha;
+        tmem_st32(tO + lane_off + c * 32, v);
+      }
+      tmem_wait_st();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t aoff = (kk >> 2) * G::kAtom + (kk & 3) * 32;
+        tc_mma_f16_ss(tO, smem_desc_sw128(sb + G::kP + aoff, 16, 1024),
+                      smem_desc_sw128(sb + G::kV + st * G::kTile + kk * 16 * 128, G::kAtom, 1024),
+                      kIdO, (j > 0 || kk > 0) ? 1u : 0u);
+      }
+      tc_commit(bar_o);
+    }
+  }
+  if (!failed && __syncthreads_or(!mbar_wait_bounded(bar_o, (n_kv - 1) & 1))) failed = true;
+
+  if (failed) {
+    if (tid == 0) set_error(kErrTimeout);
+  } else {
+    tc_fence_after();
+    const float inv = 1.f / l;
+    T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)h * D;
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      float v[32];
+      tmem_ld32(tO + lane_off + c * 32, v);
+      if (qi < len) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            pk[e] = Mma<T>::pack(v[k * 8 + 2 * e] * inv, v[k * 8 + 2 * e + 1] * inv);
+          *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, G::kTmemCols);
+  }
+}
+
 }  // namespace nb
 
 namespace nbh {
@@ -66,6 +306,39 @@ int launch_prefill_simt(const void* q, int64_t qs, const void* k, int64_t ks, co
                                                       (const T*)v, vs, hq, group, cu, sl2,
                                                       (T*)out, os);
   return check_launch("prefill_simt");
+}
+
+
+template <typename T, int D>
+int launch_prefill_tc(const void* q, int64_t qs, const void* k, int64_t ks, const void* v,
+                      int64_t vs, int hq, int hk, int group, const int32_t* cu, int B, int T_,
+                      int max_seqlen, float sl2, void* out, int64_t os, int dtype,
+                      cudaStream_t st) {
+  using G = nb::PfGeom<D>;
+  CUtensorMap qm, km, vm;
+  int rc = tensor_map_2d(&qm, q, dtype, (uint64_t)hq * D, T_, (uint64_t)qs * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
+  if (rc) return rc;
+  static bool attr_set = false;
+  auto kern = nb::prefill_tc_kernel<T, D>;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) !=
+        cudaSuccess)
+      return check_launch("prefill_tc: smem attribute");
+    attr_set = true;
+  }
+  dim3 grid((max_seqlen + 127) / 128, hq, B);
+  kern<<<grid, 128, G::kSmem, st>>>(qm, km, vm, cu, group, sl2, (T*)out, os);
+  return check_launch("prefill_tc");
+}
+
+inline bool prefill_tc_enabled() {
+  static int on = [] {
+    const char* e = getenv("NB_PREFILL_TC");  // "0" forces the SIMT kernel (diagnostics)
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
 }
 
 template <typename T>
@@ -106,6 +379,21 @@ int nb_prefill_attention(const void* q, int64_t q_stride, const void* k, int64_t
   const int group = num_q_heads / num_kv_heads;
   const float sl2 = scale * nb::kLog2e;
   cudaStream_t st = (cudaStream_t)stream;
+  const bool tc = dtype != NB_DTYPE_F32 && (head_dim == 64 || head_dim == 128) &&
+                  prefill_tc_enabled() && (q_stride * 2) % 16 == 0 && (k_stride * 2) % 16 == 0 &&
+                  (v_stride * 2) % 16 == 0 && (out_stride * 2) % 16 == 0 &&
+                  (uintptr_t)q % 16 == 0 && (uintptr_t)k % 16 == 0 && (uintptr_t)v % 16 == 0 &&
+                  (uintptr_t)out % 16 == 0;
+  if (tc) {
+#define NB_ARGS q, q_stride, k, k_stride, v, v_stride, num_q_heads, num_kv_heads, group,         \
+                cu_seqlens, num_seqs, num_tokens, max_seqlen, sl2, out, out_stride, dtype, st
+    if (dtype == NB_DTYPE_BF16)
+      return head_dim == 64 ? launch_prefill_tc<__nv_bfloat16, 64>(NB_ARGS)
+                            : launch_prefill_tc<__nv_bfloat16, 128>(NB_ARGS);
+    return head_dim == 64 ? launch_prefill_tc<__half, 64>(NB_ARGS)
+                          : launch_prefill_tc<__half, 128>(NB_ARGS);
+#undef NB_ARGS
+  }
   switch (dtype) {
     case NB_DTYPE_F32: return launch_prefill_simt_d<float>(head_dim, q, q_stride, k, k_stride, v, v_stride, num_q_heads, group, cu_seqlens, num_seqs, max_seqlen, sl2, out, out_stride, st);
     case NB_DTYPE_F16: return launch_prefill_simt_d<__half>(head_dim, q, q_stride, k, k_stride, v, v_stride, num_q_heads, group, cu_seqlens, num_seqs, max_seqlen, sl2, out, out_stride, st);

@@ -198,6 +198,8 @@ def paged_decode(q: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Ten
         raise ValueError("q must be [B, Hq, D] with unit last stride")
     if out is None:
         out = torch.empty((B, hq, d), dtype=q.dtype, device=q.device)
+    if B == 0:
+        return out
     if plan is None or plan.key != (B, hq, kvh, d, maxb, bs):
         plan = DecodePlan(B, hq, kvh, d, maxb, bs, q.device)
     ws = plan.workspace
