@@ -127,9 +127,11 @@ def test_attention_layer_prefill_then_decode(cuda, dtype, tol, H, KV, D):
                    1, False, cos_t[posd].to(cuda), sin_t[posd].to(cuda))
         assert (captured["a"].float().cpu() - a_ref.float()).abs().max().item() <= tol
     hook.remove()
-    # the whole cache is byte-identical to the reference's
-    assert torch.equal(cache.cpu().view(torch.int16 if dtype == torch.bfloat16 else torch.int32),
-                       cache_ref.view(torch.int16 if dtype == torch.bfloat16 else torch.int32))
+    # Same slots written with the same (up to GEMM rounding) rotated K/V; the
+    # byte-exact cache check with identical inputs is in test_gpu_kernels.
+    ctol = 3e-2 if dtype == torch.bfloat16 else 1e-5
+    assert (cache.float().cpu() - cache_ref.float()).abs().max().item() <= ctol
+    assert torch.equal(cache.cpu() != 0, cache_ref != 0)
 
 
 def test_runner_mixed_prefill_decode(cuda):
