@@ -131,7 +131,8 @@ def test_attention_layer_prefill_then_decode(cuda, dtype, tol, H, KV, D):
     # byte-exact cache check with identical inputs is in test_gpu_kernels.
     ctol = 3e-2 if dtype == torch.bfloat16 else 1e-5
     assert (cache.float().cpu() - cache_ref.float()).abs().max().item() <= ctol
-    assert torch.equal(cache.cpu() != 0, cache_ref != 0)
+    rows = lambda c: (c.reshape(-1, D) != 0).any(dim=1)  # noqa: E731  slots written
+    assert torch.equal(rows(cache.cpu()), rows(cache_ref))
 
 
 def test_runner_mixed_prefill_decode(cuda):
