@@ -138,6 +138,36 @@ NB_API int nb_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride
                     size_t workspace_bytes, int pages_per_split, int dtype, void* stream);
 
 /*
+ * Size in bytes of the fixed split-K scratch that nb_paged_decode_noalloc
+ * uses (16 MiB, held in the library's own device memory on every GPU that
+ * loads the library, for the life of the process).
+ */
+#define NB_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/*
+ * nb_paged_decode for callers that cannot allocate device memory: no
+ * workspace argument.  This entry point has no counterpart in needle (needle
+ * allocates its decode workspace with torch, attention.py:178-184); it exists
+ * for callers without a device allocator of their own (an FFI host with no
+ * torch), callers that must not call cudaMalloc between launches (it can
+ * synchronise the device), and callers whose device memory is fixed at
+ * start-up.  The split-K partials live in one fixed array of
+ * NB_NOALLOC_SCRATCH_BYTES inside the library; a shape whose partials do not
+ * fit is rejected with NB_ERR_INVALID_ARG and a message.  The first call on
+ * each device looks up the array's device address (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the GPU
+ * race and must be serialised by the caller.  Allocates nothing.
+ */
+NB_API int nb_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                                   const void* kv_cache, int num_blocks, int num_kv_heads,
+                                   int block_size, int head_dim, int num_q_heads,
+                                   const int32_t* block_table, int64_t block_table_stride,
+                                   int max_blocks_per_seq, const int32_t* context_lens,
+                                   int num_seqs, float scale, void* out, int64_t out_stride_seq,
+                                   int64_t out_stride_head, int pages_per_split, int dtype,
+                                   void* stream);
+
+/*
  * Causal prefill attention over each sequence's new tokens, q [T, Hq, D],
  * k/v [T, Hkv, D] (post-RoPE, token-major, row strides given), output
  * [T, Hq, D].  Replaces needle/layers/attention.py:120-134 (_prefill_pytorch)

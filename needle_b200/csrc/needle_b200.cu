@@ -8,3 +8,4 @@
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "norm.cuh"
+#include "noalloc.cuh"
