@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample budget (rank 0, N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["decode-op", "llama8b", "qwen72b"], default="decode-op",
+                    help="decode-op: config 2 (default); llama8b: config 3 at N=1, config 4 "
+                         "(tp=N) at N>1; qwen72b: config 5 (tp=N, N>=4)")
     return ap.parse_args()
 
 
@@ -383,10 +386,136 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# model workloads (configs 3-5): decode tokens/s through ModelRunner.execute
+# ---------------------------------------------------------------------------
+
+def _weights_read_per_step(runner) -> int:
+    """Bytes of weights one decode step reads on this rank: every parameter
+    except the embedding table (only B rows of it are gathered)."""
+    n = 0
+    for name, p in runner.model.named_parameters():
+        if name != "model.embed_tokens.weight":
+            n += p.numel() * p.element_size()
+    return n
+
+
+def run_model(args):
+    rank, local, ws = dist_init(args.gpus)
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    from needle_b200.model import ModelRunner, preset
+    from needle_b200.model.driver import BatchDriver, blocks_needed
+    from needle_b200.model.sequence import SamplingParams
+    from needle_b200.synth import synth_prompts
+
+    g = torch.Generator().manual_seed(0)
+    if args.workload == "llama8b":
+        cfg = preset("llama3-8b")
+        if ws == 1:
+            n_req, lo, hi, out_tokens, name = 256, 128, 1024, 256, "config3"
+        else:
+            n_req, lo, hi, out_tokens, name = 512, 256, 2048, 512, "config4"
+        prompts = synth_prompts(n_req, lo, hi, cfg.vocab_size, seed=0)
+        prefill = True
+    else:
+        cfg = preset("qwen2-72b")
+        n_req, out_tokens, name = 128, 128, "config5"
+        ctx = torch.randint(4096, 8193, (n_req,), generator=g).tolist()
+        prompts = [torch.randint(0, cfg.vocab_size, (c,), generator=g).tolist() for c in ctx]
+        prefill = False
+    runner = ModelRunner(cfg, block_size=16, dtype="bfloat16", device=str(dev),
+                         tensor_parallel_size=ws, tp_rank=rank)
+    runner.init_synthetic(seed=0)
+    nblk = blocks_needed([len(p) for p in prompts], out_tokens + 1, 16)
+    runner.init_kv_cache(nblk, 0)
+    drv = BatchDriver(runner, nblk)
+    params = SamplingParams(temperature=0.0, max_new_tokens=out_tokens)
+    seqs = [drv.add(p, params) for p in prompts]
+    st = torch.cuda.current_stream(dev)
+    t_prefill_ms = None
+    if prefill:
+        barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        drv.step()                      # one prefill forward over every prompt
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+        t_prefill_ms = e0.elapsed_time(e1)
+    else:
+        # config 5 starts from decode: a synthetic (random) cache holds each
+        # sequence's context, and one token has been "generated" already.
+        gd = torch.Generator(device=dev).manual_seed(1 + rank)
+        for c in runner.kv_caches:
+            c.normal_(generator=gd)
+        for s in seqs:
+            s.append_token(int(torch.randint(0, cfg.vocab_size, (1,), generator=g)))
+    steps_left = out_tokens - (1 if prefill else 0)
+    W = min(max(3, args.warmup), max(1, steps_left // 4))
+    K = min(args.steps, steps_left - W)
+    for _ in range(W):
+        drv.step()
+    torch.cuda.synchronize(dev)
+    ctx_sum = sum(len(s.token_ids) - 1 for s in seqs)  # tokens cached before the first timed step
+    B = len(seqs)
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    with clocks:
+        barrier(ws)
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(st)
+        for _ in range(K):
+            drv.step()
+        end.record(st)
+        torch.cuda.synchronize(dev)
+        barrier(ws)
+    t_ms = max_over_ranks(start.elapsed_time(end), ws, dev)
+    value = B * K / (t_ms / 1e3)
+    # HBM roofline of the whole step (per rank): weights + every cached K/V row
+    kvh = max(1, cfg.num_key_value_heads // ws)
+    kv_tok = 2 * kvh * cfg.head_dim * 2 * cfg.num_hidden_layers
+    avg_ctx_bytes = (ctx_sum + B * (K + 1) / 2.0) * kv_tok
+    w_bytes = _weights_read_per_step(runner)
+    step_bytes = w_bytes + avg_ctx_bytes
+    peak, peak_src = measured_hbm_peak()
+    bound = B * peak * 1e9 / step_bytes
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
+            "steps": K, "warmup": W, "ms_per_step": round(t_ms / K, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random weights and token ids)",
+            "config": {"workload": f"{name}: {cfg.model_type} "
+                                   f"{cfg.hidden_size}h/{cfg.num_hidden_layers}L decode through "
+                                   "ModelRunner.execute (host inputs, sampled tokens read back)",
+                       "model": args.workload, "batch": B, "tp": ws,
+                       "prompt_tokens": sum(len(p) for p in prompts) if prefill else None,
+                       "ctx_at_first_timed_step": round(ctx_sum / B, 1),
+                       "prefill_ms": round(t_prefill_ms, 1) if t_prefill_ms else None,
+                       "parallelism": f"tp{ws}"},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + KV per rank)",
+                         "achieved": round(step_bytes * K / (t_ms / 1e3) / 1e9, 1),
+                         "peak": peak, "unit": "GB/s",
+                         "frac": round(value / bound, 4), "peak_source": peak_src,
+                         "bytes_per_step": int(step_bytes), "weights_bytes": int(w_bytes),
+                         "tokens_per_s_bound": round(bound, 1), "traffic": None},
+            "e2e": {"value": round(value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": B * (8 + 8 + 4 + 4) + B * 4 * (len(seqs[0].token_ids) // 16 + 1),
+                    "d2h_bytes_per_step": B * 8},
+            "cpu_baseline": None, "gpu_launches": None, "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "decode-op":
+        run_model(args)
     else:
         run_ours(args)
 

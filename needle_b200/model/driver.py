@@ -14,6 +14,7 @@ run where needle itself is not installed.
 from __future__ import annotations
 
 import itertools
+from collections import deque
 from typing import List, Optional
 
 import torch
@@ -25,10 +26,9 @@ class BatchDriver:
     def __init__(self, runner, num_gpu_blocks: int, block_order: Optional[List[int]] = None):
         self.runner = runner
         self.bs = runner.block_size
-        self.free = list(block_order) if block_order is not None else list(range(num_gpu_blocks))
+        order = list(block_order) if block_order is not None else list(range(num_gpu_blocks))
         # needle pads block tables with the last block; keep it out of the free list
-        if num_gpu_blocks - 1 in self.free:
-            self.free.remove(num_gpu_blocks - 1)
+        self.free = deque(b for b in order if b != num_gpu_blocks - 1)
         self.tables = {}
         self.seqs: List[Sequence] = []
         self._ids = itertools.count(1)
@@ -41,7 +41,7 @@ class BatchDriver:
                        status=SequenceStatus.RUNNING)
         if len(self.free) < nb:
             raise MemoryError("KV pool too small for the batch")
-        self.tables[sid] = [self.free.pop(0) for _ in range(nb)]
+        self.tables[sid] = [self.free.popleft() for _ in range(nb)]
         self.seqs.append(seq)
         return seq
 
@@ -50,7 +50,7 @@ class BatchDriver:
             if s.num_generated_tokens > 0 and s.num_logical_blocks > len(self.tables[s.seq_id]):
                 if not self.free:
                     raise MemoryError("KV pool exhausted")
-                self.tables[s.seq_id].append(self.free.pop(0))
+                self.tables[s.seq_id].append(self.free.popleft())
 
     def step(self) -> List[int]:
         """One engine step over all live sequences; returns the new tokens."""
