@@ -200,6 +200,15 @@ NB_API int nb_fused_add_rmsnorm(const void* x, int64_t x_stride, const void* res
                          int64_t out_stride, void* residual_out, int64_t residual_out_stride,
                          int num_tokens, int hidden, float eps, int dtype, void* stream);
 
+/*
+ * SwiGLU activation over a fused gate/up projection: gate_up is [T, 2*I]
+ * (gate in columns [0, I), up in [I, 2I)), out[T, I] = silu(gate) * up with
+ * the rounding points of needle/model/llama.py:37 (F.silu, then the
+ * multiply, each rounded to the storage dtype).
+ */
+NB_API int nb_silu_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
+                       int num_tokens, int intermediate, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,4 +8,5 @@
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "norm.cuh"
+#include "act.cuh"
 #include "noalloc.cuh"

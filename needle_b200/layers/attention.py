@@ -22,6 +22,7 @@ import math
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from .. import ops
 from .linear import ColumnParallelLinear, RowParallelLinear
@@ -45,14 +46,43 @@ class Attention(nn.Module):
                                            tp_size=tp_size, tp_rank=tp_rank)
         self.o_proj = RowParallelLinear(H * D, config.hidden_size, tp_size=tp_size,
                                         tp_rank=tp_rank)
+        self._qkv_w = None
+        self._qkv_b = None
+
+    @torch.no_grad()
+    def fuse_qkv(self) -> None:
+        """Place the q/k/v weights (and biases) in one buffer so the three
+        projections run as one GEMM.  The parameters become views into that
+        buffer, so loading ``q_proj.weight`` etc. keeps working."""
+        projs = (self.q_proj, self.k_proj, self.v_proj)
+        self._qkv_w = torch.cat([p.weight for p in projs], dim=0)
+        o = 0
+        for p in projs:
+            n = p.weight.shape[0]
+            p.weight.data = self._qkv_w[o:o + n]
+            o += n
+        if self.q_proj.bias is not None:
+            self._qkv_b = torch.cat([p.bias for p in projs], dim=0)
+            o = 0
+            for p in projs:
+                n = p.bias.shape[0]
+                p.bias.data = self._qkv_b[o:o + n]
+                o += n
 
     def forward(self, hidden_states, positions, kv_cache, block_table, cu_seqlens,
                 context_lens, max_seqlen, is_prefill, cos, sin):
         T = hidden_states.shape[0]
         H, KV, D = self.num_heads, self.num_kv_heads, self.head_dim
-        q = self.q_proj(hidden_states).view(T, H, D)
-        k = self.k_proj(hidden_states).view(T, KV, D)
-        v = self.v_proj(hidden_states).view(T, KV, D)
+        if self._qkv_w is not None:
+            # one GEMM; q/k/v are column slices of its [T, (H + 2 KV) * D] output
+            qkv = F.linear(hidden_states, self._qkv_w, self._qkv_b)
+            q = qkv[:, :H * D].view(T, H, D)
+            k = qkv[:, H * D:(H + KV) * D].view(T, KV, D)
+            v = qkv[:, (H + KV) * D:].view(T, KV, D)
+        else:
+            q = self.q_proj(hidden_states).view(T, H, D)
+            k = self.k_proj(hidden_states).view(T, KV, D)
+            v = self.v_proj(hidden_states).view(T, KV, D)
         if is_prefill:
             ops.rope_store_kvcache(q, k, v, cos, sin, kv_cache, block_table, context_lens,
                                    cu_seqlens=cu_seqlens, write_k_back=True)

@@ -26,9 +26,8 @@ class BatchDriver:
     def __init__(self, runner, num_gpu_blocks: int, block_order: Optional[List[int]] = None):
         self.runner = runner
         self.bs = runner.block_size
-        order = list(block_order) if block_order is not None else list(range(num_gpu_blocks))
-        # needle pads block tables with the last block; keep it out of the free list
-        self.free = deque(b for b in order if b != num_gpu_blocks - 1)
+        # the runner keeps its own padding block beyond num_gpu_blocks
+        self.free = deque(block_order if block_order is not None else range(num_gpu_blocks))
         self.tables = {}
         self.seqs: List[Sequence] = []
         self._ids = itertools.count(1)
@@ -76,9 +75,8 @@ class BatchDriver:
 
 
 def blocks_needed(prompt_lens: List[int], new_tokens: int, block_size: int) -> int:
-    """KV blocks a batch needs to generate ``new_tokens`` per prompt (plus
-    the padding block)."""
-    return sum((n + new_tokens + block_size - 1) // block_size for n in prompt_lens) + 1
+    """KV blocks a batch needs to generate ``new_tokens`` per prompt."""
+    return sum((n + new_tokens + block_size - 1) // block_size for n in prompt_lens)
 
 
 def top2_margins(logits: torch.Tensor) -> List[float]:

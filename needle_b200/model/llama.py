@@ -15,6 +15,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .. import ops
 from ..layers.attention import Attention
 from ..layers.linear import ColumnParallelLinear, RowParallelLinear
 from ..layers.norm import RMSNorm
@@ -30,8 +31,20 @@ class LlamaMLP(nn.Module):
         self.gate_proj = ColumnParallelLinear(h, i, tp_size=tp_size, tp_rank=tp_rank)
         self.up_proj = ColumnParallelLinear(h, i, tp_size=tp_size, tp_rank=tp_rank)
         self.down_proj = RowParallelLinear(i, h, tp_size=tp_size, tp_rank=tp_rank)
+        self._gu_w = None
+
+    @torch.no_grad()
+    def fuse_gate_up(self) -> None:
+        """One buffer for the gate and up weights (the parameters become
+        views into it): one GEMM, then the fused SwiGLU kernel."""
+        self._gu_w = torch.cat([self.gate_proj.weight, self.up_proj.weight], dim=0)
+        n = self.gate_proj.weight.shape[0]
+        self.gate_proj.weight.data = self._gu_w[:n]
+        self.up_proj.weight.data = self._gu_w[n:]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._gu_w is not None:
+            return self.down_proj(ops.silu_mul(F.linear(x, self._gu_w)))
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -94,6 +107,12 @@ class LlamaForCausalLM(nn.Module):
         self.config = config
         self.model = self.model_cls(config, tp_size=tp_size, tp_rank=tp_rank)
         self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+
+    def fuse_projections(self) -> None:
+        """q/k/v and gate/up weights into shared buffers (one GEMM each)."""
+        for layer in self.model.layers:
+            layer.self_attn.fuse_qkv()
+            layer.mlp.fuse_gate_up()
 
     def forward(self, input_ids, positions, kv_caches, block_table, cu_seqlens, context_lens,
                 max_seqlen, is_prefill):

@@ -76,9 +76,27 @@ class Sampler:
         return out  # type: ignore[return-value]
 
 
+class _DecodeGraph:
+    """One captured decode forward for a fixed (batch, block-table width)."""
+
+    def __init__(self, B: int, width: int, dummy: int, device):
+        self.ids = torch.zeros(B, dtype=torch.long, device=device)
+        self.pos = torch.zeros(B, dtype=torch.long, device=device)
+        self.ctx = torch.zeros(B, dtype=torch.int32, device=device)
+        self.cu = torch.arange(B + 1, dtype=torch.int32, device=device)
+        self.bt = torch.full((B, width), dummy, dtype=torch.int32, device=device)
+        self.graph = torch.cuda.CUDAGraph()
+        self.logits: Optional[torch.Tensor] = None
+
+
 class ModelRunner:
+    # Block-table width granularity of captured decode graphs: the kernels'
+    # grids depend on the width, so graphs are keyed by it, rounded up.
+    GRAPH_WIDTH_STEP = 64
+
     def __init__(self, model_config: ModelConfig, block_size: int = 16, dtype: str = "bfloat16",
-                 device: str = "cuda", tensor_parallel_size: int = 1, tp_rank: int = 0):
+                 device: str = "cuda", tensor_parallel_size: int = 1, tp_rank: int = 0,
+                 cuda_graph: bool = True, fuse: bool = True):
         self.model_config = model_config
         self.block_size = block_size
         self.device = torch.device(device)
@@ -96,10 +114,16 @@ class ModelRunner:
         model.model.rotary_emb = RotaryEmbedding(
             cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta).to(self.device, self.dtype)
         model.eval()
+        if fuse:
+            model.fuse_projections()
         self.model = model
         self.sampler = Sampler()
         self.kv_caches: List[torch.Tensor] = []
         self.cpu_kv_caches: List[torch.Tensor] = []
+        self.cuda_graph = cuda_graph
+        self.padding_block = 0
+        self._graphs: Dict[tuple, _DecodeGraph] = {}
+        self._graph_pool = None
 
     # ------------------------------------------------------------------ weights
 
@@ -154,9 +178,15 @@ class ModelRunner:
         return n, n // 2
 
     def init_kv_cache(self, num_gpu_blocks: int, num_cpu_blocks: int) -> None:
+        """Per-layer caches for the allocator's ``num_gpu_blocks`` blocks plus
+        one padding block (index ``num_gpu_blocks``) that block-table rows are
+        padded with.  needle pads with its last allocatable block
+        (``needle/model/runner.py:226-229``), which its allocator can also hand
+        to a sequence; a block no allocator owns cannot alias real KV."""
         cfg = self.model_config
         kvh = max(1, cfg.num_key_value_heads // self.tp_size)
-        shape = (2, num_gpu_blocks, kvh, self.block_size, cfg.head_dim)
+        self.padding_block = num_gpu_blocks
+        shape = (2, num_gpu_blocks + 1, kvh, self.block_size, cfg.head_dim)
         self.kv_caches = [torch.zeros(shape, dtype=self.dtype, device=self.device)
                           for _ in range(cfg.num_hidden_layers)]
         self.cpu_kv_caches = []
@@ -187,8 +217,62 @@ class ModelRunner:
                              next_token_ids=self.sampler.sample(logits, params))
 
     def _forward(self, inp: ExecuteInput) -> torch.Tensor:
+        if self.cuda_graph and not inp.is_prefill:
+            return self._forward_decode_graph(inp)
         return self.model(inp.input_ids, inp.position_ids, self.kv_caches, inp.block_table,
                           inp.cu_seqlens, inp.context_lens, inp.max_seqlen, inp.is_prefill)
+
+    # ------------------------------------------------------------------ graphs
+
+    def _forward_decode_graph(self, inp: ExecuteInput) -> torch.Tensor:
+        """Decode forward through a captured CUDA graph.
+
+        The graph runs the whole model (embedding, every layer's GEMMs, fused
+        RoPE + KV write, paged decode + merge, fused residual + RMSNorm, NCCL
+        all-reduces under TP, lm_head) on static input buffers; each step
+        copies its inputs into them and replays.  Block-table columns beyond
+        the step's width point at needle's padding block, which decode never
+        reads (a sequence reads only its own ceil((ctx+1)/16) columns).
+        """
+        B, width = inp.block_table.shape
+        w = -(-width // self.GRAPH_WIDTH_STEP) * self.GRAPH_WIDTH_STEP
+        g = self._graphs.get((B, w))
+        if g is None:
+            g = self._capture_decode(B, w)
+        g.ids.copy_(inp.input_ids, non_blocking=True)
+        g.pos.copy_(inp.position_ids, non_blocking=True)
+        g.ctx.copy_(inp.context_lens, non_blocking=True)
+        g.bt[:, :width].copy_(inp.block_table, non_blocking=True)
+        g.graph.replay()
+        return g.logits
+
+    def _capture_decode(self, B: int, width: int) -> _DecodeGraph:
+        g = _DecodeGraph(B, width, self.padding_block, self.device)
+
+        def run():
+            return self.model(g.ids, g.pos, self.kv_caches, g.bt, g.cu, g.ctx, 1, False)
+
+        # Warm-up outside the graph (creates the split plan and workspace,
+        # sets kernel attributes, initialises NCCL); its KV writes land in
+        # the padding block (context 0, every table entry = padding block),
+        # which no sequence owns.
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                run()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g.graph, pool=self._graph_pool):
+            g.logits = run()
+        self._graphs[(B, width)] = g
+        return g
+
+    def release_graphs(self) -> None:
+        """Drop captured graphs (required before destroying an NCCL group)."""
+        self._graphs.clear()
+        self._graph_pool = None
 
     def _swap_kv_blocks(self, mapping: dict, direction: str) -> None:
         """Copy whole blocks between the device and pinned host caches
@@ -222,7 +306,7 @@ class ModelRunner:
             ctx.append(c)
         maxb = max((len(block_tables.get(s.seq_id, [])) for s in all_seqs), default=1)
         maxb = max(maxb, 1)
-        dummy = (self.kv_caches[0].shape[1] if self.kv_caches else 1) - 1
+        dummy = self.padding_block
         bt = [block_tables.get(s.seq_id, []) + [dummy] * (maxb - len(block_tables.get(s.seq_id, [])))
               for s in all_seqs]
         max_seqlen = max((cu[i + 1] - cu[i] for i in range(len(all_seqs))), default=1)

@@ -277,6 +277,20 @@ def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Ten
     return out, residual_out
 
 
+def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(gate_up[:, :I]) * gate_up[:, I:]`` for a fused ``[T, 2I]`` input."""
+    _cuda(gate_up, out)
+    if gate_up.dim() != 2 or gate_up.stride(1) != 1 or gate_up.shape[1] % 2:
+        raise ValueError("gate_up must be [T, 2I] with unit column stride")
+    T, two_i = gate_up.shape
+    inter = two_i // 2
+    if out is None:
+        out = torch.empty((T, inter), dtype=gate_up.dtype, device=gate_up.device)
+    L.check(L.lib().nb_silu_mul(gate_up.data_ptr(), gate_up.stride(0), out.data_ptr(),
+                                out.stride(0), T, inter, _dtype(gate_up), _stream(gate_up)))
+    return out
+
+
 def device_errors() -> int:
     """Synchronise and return (and clear) the device error word; see
     ``NB_DEVERR_*`` in the header."""

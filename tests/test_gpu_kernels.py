@@ -381,3 +381,17 @@ def test_decode_every_kernel_config(cuda, cfg):
     r = subprocess.run([sys.executable, "-c", _CFG_CHECK], cwd=root, env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_silu_mul_matches_needle_ops(cuda, dt):
+    """Fused SwiGLU vs needle's F.silu(gate) * up (llama.py:37) evaluated by
+    torch on the same device: within one unit in the last place."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(23)
+    T, I = 37, 1792
+    gu = (torch.randn(T, 2 * I, generator=g) * 3).to(dt).to(cuda)
+    ref = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    out = ops.silu_mul(gu)
+    bad, md = _ulp_close(out, ref, dt)
+    assert bad == 0, (bad, md)
