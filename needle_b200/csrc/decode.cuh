@@ -68,6 +68,10 @@ __global__ void __launch_bounds__(WARPS * 32)
                            int max_splits) {
   using G = TcGeom<D>;
   constexpr int NK = D / 16;
+  // Launched with programmatic stream serialisation: everything this grid
+  // reads (q, the cache pages, the block table, context lengths) may come
+  // from the kernel just before it, so wait for that grid first.
+  griddep_wait();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -286,6 +290,7 @@ __global__ void __launch_bounds__(128)
                              float* __restrict__ part_o, float2* __restrict__ part_ml,
                              int max_splits) {
   constexpr int EPL = D / 32;
+  griddep_wait();  // see paged_decode_tc_kernel
   extern __shared__ float sm_f[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nhc = (group + GMAX - 1) / GMAX;
@@ -450,6 +455,21 @@ __global__ void __launch_bounds__(128)
 // ---------------------------------------------------------------------------
 namespace nbh {
 
+// Launch configuration with programmatic stream serialisation (programmatic
+// dependent launch): the grid may be scheduled while the previous kernel in
+// the stream drains; its kernels call griddep_wait() before reading anything.
+inline void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[1], dim3 grid,
+                       dim3 block, size_t smem, cudaStream_t st) {
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+}
+
 // Tensor-core decode configuration: warps per CTA and TMA pipeline depth per
 // warp.  Each warp keeps one page id per lane, so a split holds at most
 // 32 * warps pages.
@@ -487,10 +507,13 @@ int launch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t
       return check_launch("paged_decode_tc: smem attribute");
     attr_set = true;
   }
-  dim3 grid(max_splits, kvh, B);
-  kern<<<grid, WARPS * 32, smem, st>>>(map, (const T*)q, qsb, qsh, bt, bts, maxb, ctx, kvh, group,
-                                       nblk, scale_log2, pps, (T*)out, osb, osh, po, pml,
-                                       max_splits);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, dim3(max_splits, kvh, B), dim3(WARPS * 32), smem, st);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, map, (const T*)q, qsb, qsh, bt, bts, maxb,
+                                           ctx, kvh, group, nblk, scale_log2, pps, (T*)out, osb,
+                                           osh, po, pml, max_splits);
+  if (e != cudaSuccess) return fail(NB_ERR_CUDA, "paged_decode_tc launch: %s", cudaGetErrorString(e));
   return check_launch("paged_decode_tc");
 }
 
@@ -528,10 +551,14 @@ int launch_decode_simt(const void* cache, int nblk, int kvh, int bs, const void*
     attr_set = true;
   }
   const int nhc = (group + GMAX - 1) / GMAX;
-  dim3 grid(max_splits, kvh * nhc, B);
-  kern<<<grid, 128, smem, st>>>((const T*)cache, nblk, kvh, bs, (const T*)q, qsb, qsh, bt, bts,
-                                maxb, ctx, group, scale_log2, pps, (T*)out, osb, osh, po, pml,
-                                max_splits);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, dim3(max_splits, kvh * nhc, B), dim3(128), smem, st);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const T*)cache, nblk, kvh, bs, (const T*)q,
+                                           qsb, qsh, bt, bts, maxb, ctx, group, scale_log2, pps,
+                                           (T*)out, osb, osh, po, pml, max_splits);
+  if (e != cudaSuccess)
+    return fail(NB_ERR_CUDA, "paged_decode_simt launch: %s", cudaGetErrorString(e));
   return check_launch("paged_decode_simt");
 }
 
@@ -557,15 +584,8 @@ int launch_merge(const float* po, const float2* pml, const int32_t* ctx, int max
                  cudaStream_t st) {
   const int pairs = B * H;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((pairs + 3) / 4);
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  pdl_config(cfg, attr, dim3((pairs + 3) / 4), dim3(128), 0, st);
   cudaError_t e = cudaLaunchKernelEx(&cfg, nb::decode_merge_kernel<T>, po, pml, ctx, maxb, bs,
                                      pps, B, H, D, max_splits, (T*)out, osb, osh);
   if (e != cudaSuccess) return fail(NB_ERR_CUDA, "decode_merge launch: %s", cudaGetErrorString(e));

@@ -12,10 +12,6 @@ namespace nb {
 // index math of needle/layers/attention.py:214-240: position = ctx + i,
 // column = position / block_size clamped to the last table column.  Returns
 // false (and records why) when the token must not be written.
-struct Slot {
-  int64_t row;  // row index of (block, head 0, offset) in the [.., block_size, D] cache
-};
-
 __device__ __forceinline__ bool token_slot(int t, const int32_t* __restrict__ cu,
                                            const int32_t* __restrict__ ctx, int num_seqs,
                                            const int32_t* __restrict__ bt, int64_t bt_stride,
@@ -59,6 +55,7 @@ __global__ void __launch_bounds__(256)
                          int block_size, int D, const int32_t* __restrict__ bt, int64_t bt_stride,
                          int maxb, const int32_t* __restrict__ cu, const int32_t* __restrict__ ctx,
                          int num_seqs, int num_tokens) {
+  griddep_launch_dependents();  // the paged decode that follows may start its launch
   constexpr int VEC = 16 / sizeof(T);
   const int vpr = D / VEC;                       // vectors per head row
   const int64_t total = (int64_t)num_tokens * kvh * 2 * vpr;
@@ -194,6 +191,7 @@ __global__ void __launch_bounds__(256)
                       const int32_t* __restrict__ bt, int64_t bt_stride, int maxb,
                       const int32_t* __restrict__ cu, const int32_t* __restrict__ ctx,
                       int num_seqs, int num_tokens, int write_k_back) {
+  griddep_launch_dependents();  // the paged decode that follows may start its launch
   const int half = D / 2;
   const int cpr = half / VEC;
   const int heads = hq + 2 * hk;
