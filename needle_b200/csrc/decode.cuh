@@ -604,15 +604,18 @@ int nb_paged_decode_plan(int num_seqs, int num_kv_heads, int max_blocks_per_seq,
   if (!pages_per_split || !max_splits) return fail(NB_ERR_INVALID_ARG, "null output pointer");
   if (num_seqs <= 0 || num_kv_heads <= 0 || max_blocks_per_seq <= 0 || block_size <= 0)
     return fail(NB_ERR_INVALID_ARG, "non-positive shape");
-  // Aim for about four waves of the three 4-warp CTAs that fit on an SM
-  // (66 KB of shared memory each).  The block-table width is the longest
-  // sequence; the batch average is assumed to be ~3/4 of it.  A sweep on
-  // B200 at config 2 (64 x 8 heads, 32..256 pages) put the optimum at 56-64
-  // pages per split; this formula gives 56 there.
+  // Splits exist only to give the GPU enough CTAs: aim for about four waves
+  // of the three 4-warp CTAs that fit on an SM (66 KB of shared memory each).
+  // When sequences x KV heads already reach that, every sequence is one
+  // split (no partials, no merge).  Otherwise the longest sequence (the
+  // block-table width) is cut into that many splits.  At config 2 (64 x 8
+  // heads, up to 256 pages) this gives 64 pages per split, the optimum of a
+  // sweep on B200; at 256 x 8 heads it gives one split.
   const int sms = num_sms();
-  const double work = 0.75 * num_seqs * (double)num_kv_heads * max_blocks_per_seq;
-  const double target = 12.0 * sms;
-  int pps = (int)((work + target - 1) / target);
+  const long long target = 12ll * sms;
+  const long long units = (long long)num_seqs * num_kv_heads;
+  const long long splits = units >= target ? 1 : (target + units - 1) / units;
+  int pps = (int)((max_blocks_per_seq + splits - 1) / splits);
   pps = (pps + 3) / 4 * 4;
   const int lo = 8 * 16 / block_size > 0 ? 8 * 16 / block_size : 1;  // >= 128 tokens per split
   if (pps < lo) pps = lo;

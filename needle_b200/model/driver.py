@@ -57,8 +57,7 @@ class BatchDriver:
         pre = [s for s in self.seqs if s.num_generated_tokens == 0]
         dec = [s for s in self.seqs if s.num_generated_tokens > 0]
         out = self.runner.execute(SchedulerOutput(prefill_seqs=pre, decode_seqs=dec,
-                                                  block_tables={k: list(v) for k, v in
-                                                                self.tables.items()},
+                                                  block_tables=self.tables,
                                                   swap_in_map={}, swap_out_map={},
                                                   blocks_to_free=[]))
         by_id = dict(zip(out.seq_ids, out.next_token_ids))

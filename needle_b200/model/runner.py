@@ -20,6 +20,7 @@ from __future__ import annotations
 
 from typing import Dict, List, Optional
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 
@@ -285,33 +286,50 @@ class ModelRunner:
             else:
                 gpu[:, dst.to(self.device)] = cpu[:, src].to(self.device, non_blocking=True)
 
-    def _h2d(self, data, dtype) -> torch.Tensor:
-        return torch.tensor(data, dtype=dtype).pin_memory().to(self.device, non_blocking=True)
+    def _h2d(self, data, dtype=None) -> torch.Tensor:
+        t = data if isinstance(data, torch.Tensor) else (
+            torch.from_numpy(data) if isinstance(data, np.ndarray) else torch.tensor(data, dtype=dtype))
+        return t.pin_memory().to(self.device, non_blocking=True)
 
     def _prepare_inputs(self, prefill_seqs, decode_seqs, block_tables) -> ExecuteInput:
+        """Same tensors as ``needle/model/runner.py:194-249``: a sequence with
+        nothing generated feeds its whole prompt at context 0, any other feeds
+        its last token at context ``length - 1``; block-table rows are padded
+        (here with the reserved padding block).  Built with numpy; pure decode
+        batches take a vectorised path."""
         all_seqs = list(prefill_seqs) + list(decode_seqs)
         is_prefill = len(decode_seqs) == 0 or len(prefill_seqs) > 0
-        ids: List[int] = []
-        pos: List[int] = []
-        cu: List[int] = [0]
-        ctx: List[int] = []
-        for seq in all_seqs:
-            if seq.num_generated_tokens == 0:
-                toks, c = seq.token_ids, 0
-            else:
-                toks, c = [seq.last_token_id], seq.length - 1
-            ids.extend(toks)
-            pos.extend(range(c, c + len(toks)))
-            cu.append(cu[-1] + len(toks))
-            ctx.append(c)
-        maxb = max((len(block_tables.get(s.seq_id, [])) for s in all_seqs), default=1)
-        maxb = max(maxb, 1)
-        dummy = self.padding_block
-        bt = [block_tables.get(s.seq_id, []) + [dummy] * (maxb - len(block_tables.get(s.seq_id, [])))
-              for s in all_seqs]
-        max_seqlen = max((cu[i + 1] - cu[i] for i in range(len(all_seqs))), default=1)
-        return ExecuteInput(input_ids=self._h2d(ids, torch.long),
-                            position_ids=self._h2d(pos, torch.long),
-                            cu_seqlens=self._h2d(cu, torch.int32), max_seqlen=max_seqlen,
-                            block_table=self._h2d(bt, torch.int32),
-                            context_lens=self._h2d(ctx, torch.int32), is_prefill=is_prefill)
+        B = len(all_seqs)
+        if B and all(s.num_generated_tokens > 0 for s in all_seqs):
+            ids = np.fromiter((s.token_ids[-1] for s in all_seqs), np.int64, B)
+            ctx = np.fromiter((len(s.token_ids) - 1 for s in all_seqs), np.int32, B)
+            pos = ctx.astype(np.int64)
+            cu = np.arange(B + 1, dtype=np.int32)
+            max_seqlen = 1
+        else:
+            ids_l: List[int] = []
+            pos_l: List[int] = []
+            cu = np.zeros(B + 1, dtype=np.int32)
+            ctx = np.zeros(B, dtype=np.int32)
+            for i, seq in enumerate(all_seqs):
+                if seq.num_generated_tokens == 0:
+                    toks, c = seq.token_ids, 0
+                else:
+                    toks, c = [seq.token_ids[-1]], len(seq.token_ids) - 1
+                ids_l.extend(toks)
+                pos_l.extend(range(c, c + len(toks)))
+                cu[i + 1] = cu[i] + len(toks)
+                ctx[i] = c
+            ids = np.asarray(ids_l, dtype=np.int64)
+            pos = np.asarray(pos_l, dtype=np.int64)
+            max_seqlen = int((cu[1:] - cu[:-1]).max()) if B else 1
+        tables = [block_tables.get(s.seq_id, []) for s in all_seqs]
+        maxb = max(1, max(map(len, tables), default=1))
+        bt = np.full((B, maxb), self.padding_block, dtype=np.int32)
+        for i, t in enumerate(tables):
+            if t:
+                bt[i, :len(t)] = t
+        return ExecuteInput(input_ids=self._h2d(ids), position_ids=self._h2d(pos),
+                            cu_seqlens=self._h2d(cu), max_seqlen=max_seqlen,
+                            block_table=self._h2d(bt), context_lens=self._h2d(ctx),
+                            is_prefill=is_prefill)
