@@ -293,6 +293,277 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Tensor-core prefill, warp-specialised (bf16/fp16, head_dim 64/128).
+//
+// One CTA per (256 query rows, query head, sequence) holding two 128-row Q
+// tiles, A and B, that share every K/V tile.  Nine warps:
+//   warps 0-3  softmax for tile A (thread = query row = TMEM lane)
+//   warps 4-7  softmax for tile B
+//   warp 8     TMA producer and tcgen05 MMA issuer (lane 0)
+// Tensor memory (512 columns): S_A [0,128), S_B [128,256), O_A [256, 256+D),
+// O_B [256+D, 256+2D).  Per KV tile j the issuer runs S_A = Q_A K_j^T and
+// S_B = Q_B K_j^T back to back; while the tensor core works on S_B, the A
+// warps turn S_A into probabilities and write them as bf16/fp16 pairs back
+// over S_A's first 64 columns (tcgen05.st); the issuer then runs
+// O_A += P_A V_j with P_A read straight from tensor memory, and the same for
+// B.  So the two softmax groups and the tensor core take turns instead of
+// waiting for each other, no P tile goes through shared memory, and the
+// only shared-memory traffic is TMA-loaded Q, K and V (2-stage K/V ring).
+// The running max is raised lazily as in prefill_tc_kernel.  The commit
+// that signals S_X(j) also covers O_X += P_X V_{j-1}, so a softmax group may
+// rescale its O rows as soon as it sees S_X(j).  Every wait is bounded and
+// an abort flag lets all roles leave together.
+// ---------------------------------------------------------------------------
+template <int D> struct Pf2Geom {
+  static constexpr int kAtom = 128 * 128;
+  static constexpr int kTile = (D / 64) * kAtom;
+  static constexpr int kQA = 0;
+  static constexpr int kQB = kTile;
+  static constexpr int kK = 2 * kTile;          // 2 stages
+  static constexpr int kV = kK + 2 * kTile;     // 2 stages
+  static constexpr int kBars = kV + 2 * kTile;
+  static constexpr int kSmem = kBars + 128 + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kSA = 0, kSB = 128, kOA = 256, kOB = 256 + D;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(288, 1)
+    prefill_tc2_kernel(const __grid_constant__ CUtensorMap qmap,
+                       const __grid_constant__ CUtensorMap kmap,
+                       const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
+                       int group, float scale_log2, T* __restrict__ out, int64_t os) {
+  using G = Pf2Geom<D>;
+  constexpr bool kBf16 = !__is_same(T, __half);
+  constexpr uint32_t kIdS = idesc_f16_f32(kBf16, 128, 128, false, false);
+  constexpr uint32_t kIdO = idesc_f16_f32(kBf16, 128, D, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int s0 = __ldg(cu + b), len = __ldg(cu + b + 1) - s0;
+  const int q0 = qt * 256;
+  if (q0 >= len) return;
+  const bool hasB = q0 + 128 < len;
+  const int nA = 2 * qt + 1;                 // KV tiles under tile A's rows (causal)
+  const int nB = hasB ? 2 * qt + 2 : 0;
+  const int n_kv = hasB ? nB : nA;
+  const int kh = h / group;
+  const uint32_t sb = smem_u32(smem);
+  // barriers: q, kv[2], kvfree[2], sA, sB, pA, pB, done
+  const uint32_t bar_q = sb + G::kBars;
+  const uint32_t bar_kv = bar_q + 8, bar_free = bar_q + 24;
+  const uint32_t bar_sA = bar_q + 40, bar_sB = bar_q + 48;
+  const uint32_t bar_pA = bar_q + 56, bar_pB = bar_q + 64, bar_done = bar_q + 72;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G::kBars + 96);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kBars + 104);
+
+  if (warp == 8) {
+    tmem_alloc(smem_u32(tmem_slot), G::kTmemCols);
+    tmem_relinquish();
+    if (lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      mbar_init(bar_q, 1);
+      mbar_init(bar_kv, 1);
+      mbar_init(bar_kv + 8, 1);
+      mbar_init(bar_free, 1);
+      mbar_init(bar_free + 8, 1);
+      mbar_init(bar_sA, 1);
+      mbar_init(bar_sB, 1);
+      mbar_init(bar_pA, 128);
+      mbar_init(bar_pB, 128);
+      mbar_init(bar_done, 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ---------------- producer + MMA issuer ----------------
+      auto fail_out = [&]() { *abort_flag = 1; set_error(kErrTimeout); };
+      auto load_kv = [&](int j) {
+        const int st = j & 1;
+        mbar_arrive_expect_tx(bar_kv + 8 * st, 2 * G::kTile);
+#pragma unroll
+        for (int a = 0; a < D / 64; ++a) {
+          tma_load_2d(sb + G::kK + st * G::kTile + a * G::kAtom, &kmap, kh * D + a * 64,
+                      s0 + j * 128, bar_kv + 8 * st);
+          tma_load_2d(sb + G::kV + st * G::kTile + a * G::kAtom, &vmap, kh * D + a * 64,
+                      s0 + j * 128, bar_kv + 8 * st);
+        }
+      };
+      mbar_arrive_expect_tx(bar_q, (hasB ? 2 : 1) * G::kTile);
+#pragma unroll
+      for (int a = 0; a < D / 64; ++a) {
+        tma_load_2d(sb + G::kQA + a * G::kAtom, &qmap, h * D + a * 64, s0 + q0, bar_q);
+        if (hasB) tma_load_2d(sb + G::kQB + a * G::kAtom, &qmap, h * D + a * 64, s0 + q0 + 128, bar_q);
+      }
+      load_kv(0);
+      if (n_kv > 1) load_kv(1);
+      bool ok = mbar_wait_bounded(bar_q, 0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait_bounded(bar_kv + 8 * st, (j >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const bool aA = j < nA;
+        const uint32_t kst = sb + G::kK + st * G::kTile;
+        const uint32_t vst = sb + G::kV + st * G::kTile;
+        if (aA) {
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
+            tc_mma_f16_ss(tmem + G::kSA, smem_desc_sw128(sb + G::kQA + off, 16, 1024),
+                          smem_desc_sw128(kst + off, 16, 1024), kIdS, kk > 0);
+          }
+          tc_commit(bar_sA);
+        }
+        if (hasB) {
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
+            tc_mma_f16_ss(tmem + G::kSB, smem_desc_sw128(sb + G::kQB + off, 16, 1024),
+                          smem_desc_sw128(kst + off, 16, 1024), kIdS, kk > 0);
+          }
+          tc_commit(bar_sB);
+        }
+        // refill the other stage once the previous tile's MMAs released it
+        if (j >= 1 && j + 1 < n_kv) {
+          if (!mbar_wait_bounded(bar_free + 8 * ((j + 1) & 1), ((j - 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          load_kv(j + 1);
+        }
+        if (aA) {
+          if (!mbar_wait_bounded(bar_pA, j & 1) || *abort_flag) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            tc_mma_f16_ts(tmem + G::kOA, tmem + G::kSA + kk * 8,
+                          smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (hasB) {
+          if (!mbar_wait_bounded(bar_pB, j & 1) || *abort_flag) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            tc_mma_f16_ts(tmem + G::kOB, tmem + G::kSB + kk * 8,
+                          smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(bar_free + 8 * st);
+      }
+      if (!ok) fail_out();
+      tc_commit(bar_done);
+    }
+  } else {
+    // ---------------- softmax groups ----------------
+    const int wg = warp >> 2;  // 0 = tile A, 1 = tile B
+    const int n_mine = wg ? nB : nA;
+    const uint32_t tSx = tmem + (wg ? G::kSB : G::kSA);
+    const uint32_t tOx = tmem + (wg ? G::kOB : G::kOA);
+    const uint32_t bar_s = wg ? bar_sB : bar_sA;
+    const uint32_t bar_p = wg ? bar_pB : bar_pA;
+    const int r = (warp & 3) * 32 + lane;
+    const int qi = q0 + wg * 128 + r;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < n_mine; ++j) {
+      const bool got = mbar_wait_bounded(bar_s, j & 1);
+      if (__any_sync(0xffffffffu, !got) || *abort_flag) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int kb = j * 128;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tSx + lane_off + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = kb + c * 32 + i;
+          if (col <= qi && col < len) mx = fmaxf(mx, v[i] * scale_log2);
+        }
+      }
+      const bool need = mx > m + kRescaleThreshold;
+      float alpha = 1.f;
+      if (need) {
+        alpha = exp2f(m - mx);
+        m = mx;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(tOx + lane_off + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st32(tOx + lane_off + c * 32, v);
+        }
+      }
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tSx + lane_off + c * 32, v);
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int col = kb + c * 32 + 2 * e;
+          const float p0 = (col <= qi && col < len) ? exp2f(v[2 * e] * scale_log2 - m) : 0.f;
+          const float p1 =
+              (col + 1 <= qi && col + 1 < len) ? exp2f(v[2 * e + 1] * scale_log2 - m) : 0.f;
+          rs += p0 + p1;
+          pk[e] = Mma<T>::pack(p0, p1);
+        }
+        tmem_st16(tSx + lane_off + c * 16, pk);  // P over S's first 64 columns
+      }
+      tmem_wait_st();
+      l = l * alpha + rs;
+      tc_fence_before();
+      mbar_arrive(bar_p);
+    }
+    const bool done = mbar_wait_bounded(bar_done, 0);
+    if (n_mine > 0 && done && !*abort_flag) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(tOx + lane_off + c * 32, v);
+        if (qi < len) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pk[e] = Mma<T>::pack(v[k * 8 + 2 * e] * inv, v[k * 8 + 2 * e + 1] * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, G::kTmemCols);
+  }
+}
+
 }  // namespace nb
 
 namespace nbh {
@@ -331,6 +602,39 @@ int launch_prefill_tc(const void* q, int64_t qs, const void* k, int64_t ks, cons
   dim3 grid((max_seqlen + 127) / 128, hq, B);
   kern<<<grid, 128, G::kSmem, st>>>(qm, km, vm, cu, group, sl2, (T*)out, os);
   return check_launch("prefill_tc");
+}
+
+
+template <typename T, int D>
+int launch_prefill_tc2(const void* q, int64_t qs, const void* k, int64_t ks, const void* v,
+                       int64_t vs, int hq, int hk, int group, const int32_t* cu, int B, int T_,
+                       int max_seqlen, float sl2, void* out, int64_t os, int dtype,
+                       cudaStream_t st) {
+  using G = nb::Pf2Geom<D>;
+  CUtensorMap qm, km, vm;
+  int rc = tensor_map_2d(&qm, q, dtype, (uint64_t)hq * D, T_, (uint64_t)qs * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
+  if (rc) return rc;
+  static bool attr_set = false;
+  auto kern = nb::prefill_tc2_kernel<T, D>;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) !=
+        cudaSuccess)
+      return check_launch("prefill_tc2: smem attribute");
+    attr_set = true;
+  }
+  dim3 grid((max_seqlen + 255) / 256, hq, B);
+  kern<<<grid, 288, G::kSmem, st>>>(qm, km, vm, cu, group, sl2, (T*)out, os);
+  return check_launch("prefill_tc2");
+}
+
+inline int prefill_version() {
+  static int v = [] {
+    const char* e = getenv("NB_PREFILL_V");  // "1": single-group kernel (diagnostics)
+    return (e && e[0] == '1') ? 1 : 2;
+  }();
+  return v;
 }
 
 inline bool prefill_tc_enabled() {
@@ -387,6 +691,13 @@ int nb_prefill_attention(const void* q, int64_t q_stride, const void* k, int64_t
   if (tc) {
 #define NB_ARGS q, q_stride, k, k_stride, v, v_stride, num_q_heads, num_kv_heads, group,         \
                 cu_seqlens, num_seqs, num_tokens, max_seqlen, sl2, out, out_stride, dtype, st
+    if (prefill_version() == 2) {
+      if (dtype == NB_DTYPE_BF16)
+        return head_dim == 64 ? launch_prefill_tc2<__nv_bfloat16, 64>(NB_ARGS)
+                              : launch_prefill_tc2<__nv_bfloat16, 128>(NB_ARGS);
+      return head_dim == 64 ? launch_prefill_tc2<__half, 64>(NB_ARGS)
+                            : launch_prefill_tc2<__half, 128>(NB_ARGS);
+    }
     if (dtype == NB_DTYPE_BF16)
       return head_dim == 64 ? launch_prefill_tc<__nv_bfloat16, 64>(NB_ARGS)
                             : launch_prefill_tc<__nv_bfloat16, 128>(NB_ARGS);

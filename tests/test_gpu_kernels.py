@@ -395,3 +395,42 @@ def test_silu_mul_matches_needle_ops(cuda, dt):
     out = ops.silu_mul(gu)
     bad, md = _ulp_close(out, ref, dt)
     assert bad == 0, (bad, md)
+
+
+_PREFILL_CHECK = r"""
+import math, sys, numpy as np, torch
+sys.path.insert(0, '.')
+from needle_b200 import ops
+from oracle import needle_oracle as no
+g = torch.Generator().manual_seed(29)
+for dt in (torch.bfloat16, torch.float16):
+    for H, kv, D in ((32, 8, 128), (14, 2, 64), (4, 4, 128)):
+        lens = [1, 127, 128, 129, 255, 256, 257, 600, 0, 64]
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32)
+        T = int(cu[-1])
+        q = torch.randn(T, H, D, generator=g).to(dt)
+        k = torch.randn(T, kv, D, generator=g).to(dt)
+        v = torch.randn(T, kv, D, generator=g).to(dt)
+        ref = no.prefill_attention(q.float(), k.float(), v.float(), cu, H, kv)
+        dev = torch.device('cuda:0')
+        out = ops.prefill_attention(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), max(lens))
+        err = (out.float().cpu() - ref).abs().max().item()
+        assert err <= 2e-2, (dt, H, kv, D, err)
+assert ops.device_errors() == 0
+print('ok')
+"""
+
+
+@pytest.mark.parametrize("version", ["1", "2"])
+def test_prefill_every_kernel_version(cuda, version):
+    """Both tensor-core prefill kernels (single softmax group / two ping-pong
+    groups), selected through NB_PREFILL_V in a fresh process, on lengths
+    around the 128- and 256-row tile edges, bf16 and fp16."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NB_PREFILL_V=version)
+    r = subprocess.run([sys.executable, "-c", _PREFILL_CHECK], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
