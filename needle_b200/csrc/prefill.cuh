@@ -410,59 +410,67 @@ __global__ void __launch_bounds__(288, 1)
       }
       load_kv(0);
       if (n_kv > 1) load_kv(1);
-      bool ok = mbar_wait_bounded(bar_q, 0);
+      // Issue order: S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) S_A(2) ...
+      // so that group A's softmax of tile j+1 overlaps group B's softmax of
+      // tile j and the tensor core's P_B.V_j.
+      int kv_ready = -1;  // highest KV tile whose load has been waited for
+      auto wait_kv = [&](int j) -> bool {
+        if (j <= kv_ready) return true;
+        if (!mbar_wait_bounded(bar_kv + 8 * (j & 1), (j >> 1) & 1)) return false;
+        kv_ready = j;
+        tc_fence_after();
+        return true;
+      };
+      auto issue_s = [&](int j, uint32_t q_off, uint32_t t_col, uint32_t bar) {
+        const uint32_t kst = sb + G::kK + (j & 1) * G::kTile;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
+          tc_mma_f16_ss(tmem + t_col, smem_desc_sw128(sb + q_off + off, 16, 1024),
+                        smem_desc_sw128(kst + off, 16, 1024), kIdS, kk > 0);
+        }
+        tc_commit(bar);
+      };
+      auto issue_pv = [&](int j, uint32_t s_col, uint32_t o_col) {
+        const uint32_t vst = sb + G::kV + (j & 1) * G::kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16_ts(tmem + o_col, tmem + s_col + kk * 8,
+                        smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait_bounded(bar_q, 0) && wait_kv(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, G::kQA, G::kSA, bar_sA);
+        if (hasB) issue_s(0, G::kQB, G::kSB, bar_sB);
+      }
       for (int j = 0; ok && j < n_kv; ++j) {
         const int st = j & 1;
-        if (!mbar_wait_bounded(bar_kv + 8 * st, (j >> 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        const bool aA = j < nA;
-        const uint32_t kst = sb + G::kK + st * G::kTile;
-        const uint32_t vst = sb + G::kV + st * G::kTile;
-        if (aA) {
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
-            tc_mma_f16_ss(tmem + G::kSA, smem_desc_sw128(sb + G::kQA + off, 16, 1024),
-                          smem_desc_sw128(kst + off, 16, 1024), kIdS, kk > 0);
-          }
-          tc_commit(bar_sA);
-        }
-        if (hasB) {
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
-            tc_mma_f16_ss(tmem + G::kSB, smem_desc_sw128(sb + G::kQB + off, 16, 1024),
-                          smem_desc_sw128(kst + off, 16, 1024), kIdS, kk > 0);
-          }
-          tc_commit(bar_sB);
-        }
-        // refill the other stage once the previous tile's MMAs released it
-        if (j >= 1 && j + 1 < n_kv) {
-          if (!mbar_wait_bounded(bar_free + 8 * ((j + 1) & 1), ((j - 1) >> 1) & 1)) {
-            ok = false;
-            break;
-          }
-          load_kv(j + 1);
-        }
-        if (aA) {
+        if (j < nA) {
           if (!mbar_wait_bounded(bar_pA, j & 1) || *abort_flag) { ok = false; break; }
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            tc_mma_f16_ts(tmem + G::kOA, tmem + G::kSA + kk * 8,
-                          smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
-                          (j > 0 || kk > 0) ? 1u : 0u);
+          issue_pv(j, G::kSA, G::kOA);
+          if (j + 1 < nA) {
+            if (!wait_kv(j + 1)) { ok = false; break; }
+            issue_s(j + 1, G::kQA, G::kSA, bar_sA);
+          }
         }
-        if (hasB) {
+        if (j < nB) {
           if (!mbar_wait_bounded(bar_pB, j & 1) || *abort_flag) { ok = false; break; }
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            tc_mma_f16_ts(tmem + G::kOB, tmem + G::kSB + kk * 8,
-                          smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
-                          (j > 0 || kk > 0) ? 1u : 0u);
+          issue_pv(j, G::kSB, G::kOB);
+          if (j + 1 < nB) {
+            if (!wait_kv(j + 1)) { ok = false; break; }
+            issue_s(j + 1, G::kQB, G::kSB, bar_sB);
+          }
         }
         tc_commit(bar_free + 8 * st);
+        // refill this stage with tile j+2 once tile j's MMAs have released it
+        if (j + 2 < n_kv) {
+          if (!mbar_wait_bounded(bar_free + 8 * st, (j >> 1) & 1)) { ok = false; break; }
+          load_kv(j + 2);
+        }
       }
       if (!ok) fail_out();
       tc_commit(bar_done);
