@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample budget (rank 0, N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode-op", "llama8b", "qwen72b"], default="decode-op",
+    ap.add_argument("--workload", choices=["decode-op", "llama8b", "qwen72b", "prefill"],
+                    default="decode-op",
                     help="decode-op: config 2 (default); llama8b: config 3 at N=1, config 4 "
                          "(tp=N) at N>1; qwen72b: config 5 (tp=N, N>=4)")
     return ap.parse_args()
@@ -502,9 +503,86 @@ def run_model(args):
             "e2e": {"value": round(value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": B * (8 + 8 + 4 + 4) + B * 4 * (len(seqs[0].token_ids) // 16 + 1),
                     "d2h_bytes_per_step": B * 8},
-            "cpu_baseline": None, "gpu_launches": None, "clocks": clocks.summary(),
+            "cpu_baseline": None,
+            # our kernels per decode step: first RMSNorm, per layer RoPE+KV-write,
+            # paged decode (+ merge when split), 2 fused add+RMSNorm, SwiGLU
+            "gpu_launches": K * (cfg.num_hidden_layers * (5 + (1 if _splits(runner, seqs) > 1 else 0)) + 1),
+            "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    runner.release_graphs()
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _splits(runner, seqs) -> int:
+    """Splits per sequence the decode plan uses for this batch shape."""
+    import ctypes
+    from needle_b200 import _lib as L
+    cfg = runner.model_config
+    kvh = max(1, cfg.num_key_value_heads // runner.tp_size)
+    maxb = max(len(s.token_ids) for s in seqs) // 16 + 1
+    pps, ms = ctypes.c_int(0), ctypes.c_int(0)
+    L.check(L.lib().nb_paged_decode_plan(len(seqs), kvh, maxb, 16, ctypes.byref(pps),
+                                         ctypes.byref(ms)))
+    return ms.value
+
+
+# ---------------------------------------------------------------------------
+# prefill workload: the tcgen05 prefill kernel alone (tensor-pipe roofline)
+# ---------------------------------------------------------------------------
+
+def run_prefill(args):
+    """Causal prefill attention of 16 sequences x 1024 new tokens, 32/8 heads,
+    D=128, bf16 (the config 3 head geometry); reports TFLOP/s against the
+    measured dense bf16 peak."""
+    rank, local, ws = dist_init(args.gpus)
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    from needle_b200 import ops
+    B, S, H, KV, D = 16, 1024, 32, 8, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    T = B * S
+    q = torch.randn(T, H, D, device=dev, generator=g, dtype=torch.bfloat16)
+    k = torch.randn(T, KV, D, device=dev, generator=g, dtype=torch.bfloat16)
+    v = torch.randn(T, KV, D, device=dev, generator=g, dtype=torch.bfloat16)
+    cu = torch.arange(0, T + 1, S, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    for _ in range(max(3, args.warmup)):
+        ops.prefill_attention(q, k, v, cu, S, out=out)
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    K = args.steps
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    with clocks:
+        barrier(ws)
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(st)
+        for _ in range(K):
+            ops.prefill_attention(q, k, v, cu, S, out=out)
+        e0.record(st)
+        torch.cuda.synchronize(dev)
+        barrier(ws)
+    t_ms = max_over_ranks(s0.elapsed_time(e0), ws, dev)
+    flops = B * 4 * (S * (S + 1) / 2) * H * D
+    tflops = flops * K / (t_ms / 1e3) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        peak, src = 1590.0, "fallback"
+    if rank == 0:
+        print(json.dumps({
+            "metric": "causal prefill attention TFLOP/s", "value": round(tflops, 1),
+            "unit": "TFLOP/s", "n_gpus": ws, "steps": K, "warmup": max(3, args.warmup),
+            "ms_per_step": round(t_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,1))",
+            "config": {"workload": "prefill: 16 x 1024 new tokens, 32/8 heads, D=128, causal"},
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
+                         "peak_source": src, "flops_per_call": flops, "traffic": None},
+            "gpu_launches": K, "clocks": clocks.summary()}), flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -514,6 +592,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     elif args.workload != "decode-op":
         run_model(args)
     else:

@@ -312,6 +312,14 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(bool bf16, int M, int N, bo
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// 2^x with the hardware approximation instruction (flush-to-zero); used for
+// softmax probabilities, which are rounded to bf16/fp16 right after.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

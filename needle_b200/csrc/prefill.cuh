@@ -492,17 +492,25 @@ __global__ void __launch_bounds__(288, 1)
       if (__any_sync(0xffffffffu, !got) || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
       const int kb = j * 128;
+      // whole tile below the diagonal and inside the sequence: no masking
+      const bool full = kb + 127 <= qi && kb + 128 <= len;
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float v[32];
         tmem_ld32(tSx + lane_off + c * 32, v);
+        if (full) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = kb + c * 32 + i;
-          if (col <= qi && col < len) mx = fmaxf(mx, v[i] * scale_log2);
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = kb + c * 32 + i;
+            mx = fmaxf(mx, (col <= qi && col < len) ? v[i] : -INFINITY);
+          }
         }
       }
+      mx *= scale_log2;  // scale > 0: max of scaled scores = scaled max
       const bool need = mx > m + kRescaleThreshold;
       float alpha = 1.f;
       if (need) {
@@ -519,20 +527,31 @@ __global__ void __launch_bounds__(288, 1)
           tmem_st32(tOx + lane_off + c * 32, v);
         }
       }
+      const float neg_m = -m;
       float rs = 0.f;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float v[32];
         tmem_ld32(tSx + lane_off + c * 32, v);
         uint32_t pk[16];
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int col = kb + c * 32 + 2 * e;
-          const float p0 = (col <= qi && col < len) ? exp2f(v[2 * e] * scale_log2 - m) : 0.f;
-          const float p1 =
-              (col + 1 <= qi && col + 1 < len) ? exp2f(v[2 * e + 1] * scale_log2 - m) : 0.f;
-          rs += p0 + p1;
-          pk[e] = Mma<T>::pack(p0, p1);
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_approx(fmaf(v[2 * e], scale_log2, neg_m));
+            const float p1 = ex2_approx(fmaf(v[2 * e + 1], scale_log2, neg_m));
+            rs += p0 + p1;
+            pk[e] = Mma<T>::pack(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int col = kb + c * 32 + 2 * e;
+            const float p0 = (col <= qi && col < len) ? ex2_approx(fmaf(v[2 * e], scale_log2, neg_m)) : 0.f;
+            const float p1 = (col + 1 <= qi && col + 1 < len)
+                                 ? ex2_approx(fmaf(v[2 * e + 1], scale_log2, neg_m)) : 0.f;
+            rs += p0 + p1;
+            pk[e] = Mma<T>::pack(p0, p1);
+          }
         }
         tmem_st16(tSx + lane_off + c * 16, pk);  // P over S's first 64 columns
       }
