@@ -118,7 +118,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
 }
 
 // 2-D tiled TMA load global -> shared, completion counted on `bar` in bytes.
-// No multicast: every CTA fetches its own tiles.
+// Each CTA fetches its own tiles (one destination CTA per copy).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar) {
   asm volatile(

@@ -18,6 +18,7 @@ per sequence, ``needle/model/sampler.py:27-28``).
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, List, Optional
 
 import numpy as np
@@ -121,6 +122,9 @@ class ModelRunner:
         self.sampler = Sampler()
         self.kv_caches: List[torch.Tensor] = []
         self.cpu_kv_caches: List[torch.Tensor] = []
+        # Graph capture of the NCCL all-reduces is opt-in under TP (NB_TP_GRAPH=1).
+        if tensor_parallel_size > 1 and os.environ.get("NB_TP_GRAPH", "0") != "1":
+            cuda_graph = False
         self.cuda_graph = cuda_graph
         self.padding_block = 0
         self._graphs: Dict[tuple, _DecodeGraph] = {}
