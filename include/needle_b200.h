@@ -201,6 +201,22 @@ NB_API int nb_fused_add_rmsnorm(const void* x, int64_t x_stride, const void* res
                          int num_tokens, int hidden, float eps, int dtype, void* stream);
 
 /*
+ * Copy whole KV blocks between two paged caches of num_layers layers, e.g.
+ * the device cache and a pinned host cache (swap-out / swap-in), in one
+ * launch.  Replaces needle/model/runner.py:175-192 (_swap_kv_blocks, one
+ * .to() per block per layer).  src_caches / dst_caches: host arrays of
+ * num_layers cache base pointers (device memory or pinned host memory, both
+ * addressable by the GPU); block_pairs: num_pairs (src block, dst block)
+ * int32 pairs in GPU-addressable memory; block_bytes: bytes of one block's
+ * K (or V) half = num_kv_heads * block_size * head_dim * element size.
+ * Out-of-range block ids are skipped and recorded (NB_DEVERR_BLOCK_ID).
+ */
+NB_API int nb_swap_kv_blocks(const void* const* src_caches, void* const* dst_caches,
+                             int num_layers, const int32_t* block_pairs, int num_pairs,
+                             int64_t src_num_blocks, int64_t dst_num_blocks, int64_t block_bytes,
+                             void* stream);
+
+/*
  * SwiGLU activation over a fused gate/up projection: gate_up is [T, 2*I]
  * (gate in columns [0, I), up in [I, 2I)), out[T, I] = silu(gate) * up with
  * the rounding points of needle/model/llama.py:37 (F.silu, then the

@@ -434,12 +434,24 @@ __global__ void __launch_bounds__(128)
     const float2 ml = sl < n_splits ? part_ml[base + sl] : make_float2(-INFINITY, 0.f);
     const float wl = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
     const int cnt = min(32, n_splits - s0);
-    for (int j = 0; j < cnt; ++j) {
-      const float w = __shfl_sync(0xffffffffu, wl, j);
-      const float* src = part_o + (base + s0 + j) * D + lane * epl;
+    // four splits per step with their loads issued together (one round trip)
+    for (int j = 0; j < cnt; j += 4) {
+      float w[4], x[4][8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (e < epl) acc[e] = fmaf(src[e], w, acc[e]);
+      for (int u = 0; u < 4; ++u) {
+        const int jj = min(j + u, cnt - 1);
+        w[u] = __shfl_sync(0xffffffffu, wl, jj);
+        if (j + u >= cnt) w[u] = 0.f;
+        const float* src = part_o + (base + s0 + jj) * D + lane * epl;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < epl) x[u][e] = __ldg(src + e);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < epl) acc[e] = fmaf(x[u][e], w[u], acc[e]);
     }
   }
   T* dst = out + (int64_t)b * o_sb + (int64_t)qh * o_sh + lane * epl;

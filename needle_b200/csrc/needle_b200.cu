@@ -9,4 +9,5 @@
 #include "prefill.cuh"
 #include "norm.cuh"
 #include "act.cuh"
+#include "swap.cuh"
 #include "noalloc.cuh"

@@ -15,7 +15,7 @@
 namespace nb {
 
 template <typename T, int VEC, bool ADD>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(1024)
     rmsnorm_kernel(const T* x, int64_t xs, const T* res, int64_t rs, const T* __restrict__ w,
                    T* out, int64_t os, T* res_out, int64_t ros, int hidden, float eps) {
   __shared__ float red[32];
@@ -107,9 +107,11 @@ int launch_norm(const void* x, int64_t xs, const void* res, int64_t rs, const vo
                       (!ADD || (rs % V16 == 0 && ros % V16 == 0)) && (uintptr_t)x % 16 == 0 &&
                       (uintptr_t)w % 16 == 0 && (uintptr_t)out % 16 == 0 &&
                       (!ADD || ((uintptr_t)res % 16 == 0 && (uintptr_t)ro % 16 == 0));
-  int threads = 256;
+  // One CTA per row and (up to 1024) one vector per thread, so each thread's
+  // chain of loads is short: the kernel is latency-bound at decode batch sizes.
   const int nvec = vec_ok ? hidden / V16 : hidden;
-  while (threads > 32 && threads / 2 >= nvec) threads /= 2;
+  int threads = 32;
+  while (threads < 1024 && threads < nvec) threads *= 2;
   if (vec_ok)
     nb::rmsnorm_kernel<T, V16, ADD><<<T_, threads, 0, st>>>((const T*)x, xs, (const T*)res, rs,
                                                             (const T*)w, (T*)out, os, (T*)ro, ros,

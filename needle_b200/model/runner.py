@@ -122,8 +122,9 @@ class ModelRunner:
         self.sampler = Sampler()
         self.kv_caches: List[torch.Tensor] = []
         self.cpu_kv_caches: List[torch.Tensor] = []
-        # Graph capture of the NCCL all-reduces is opt-in under TP (NB_TP_GRAPH=1).
-        if tensor_parallel_size > 1 and os.environ.get("NB_TP_GRAPH", "0") != "1":
+        # Under TP the graph also holds the NCCL all-reduces; NB_TP_GRAPH=0
+        # turns capture off there (diagnostics).
+        if tensor_parallel_size > 1 and os.environ.get("NB_TP_GRAPH", "1") == "0":
             cuda_graph = False
         self.cuda_graph = cuda_graph
         self.padding_block = 0
@@ -281,14 +282,18 @@ class ModelRunner:
 
     def _swap_kv_blocks(self, mapping: dict, direction: str) -> None:
         """Copy whole blocks between the device and pinned host caches
-        (``needle/model/runner.py:175-192``), one gathered copy per layer."""
-        src = torch.tensor(list(mapping.keys()), dtype=torch.long)
-        dst = torch.tensor(list(mapping.values()), dtype=torch.long)
-        for gpu, cpu in zip(self.kv_caches, self.cpu_kv_caches):
-            if direction == "gpu_to_cpu":
-                cpu[:, dst] = gpu[:, src.to(self.device)].cpu()
-            else:
-                gpu[:, dst.to(self.device)] = cpu[:, src].to(self.device, non_blocking=True)
+        (``needle/model/runner.py:175-192``): every layer and block in one
+        ``nb_swap_kv_blocks`` launch.  ``mapping`` is {source block: target
+        block} (gpu->cpu for swap-out, cpu->gpu for swap-in, as in needle)."""
+        if not mapping:
+            return
+        from .. import ops
+        pairs = torch.tensor(list(mapping.items()), dtype=torch.int32).pin_memory()
+        pairs = pairs.to(self.device, non_blocking=True)
+        if direction == "gpu_to_cpu":
+            ops.swap_kv_blocks(self.kv_caches, self.cpu_kv_caches, pairs)
+        else:
+            ops.swap_kv_blocks(self.cpu_kv_caches, self.kv_caches, pairs)
 
     def _h2d(self, data, dtype=None) -> torch.Tensor:
         t = data if isinstance(data, torch.Tensor) else (

@@ -291,6 +291,34 @@ def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch
     return out
 
 
+def swap_kv_blocks(src_caches, dst_caches, pairs: torch.Tensor) -> None:
+    """Copy blocks ``pairs[i, 0]`` of every layer's ``src_caches`` to blocks
+    ``pairs[i, 1]`` of ``dst_caches`` (device <-> pinned host), one launch.
+
+    ``pairs`` is an int32 ``[n, 2]`` tensor on the device.
+    """
+    import ctypes
+    if len(src_caches) != len(dst_caches) or not src_caches:
+        raise ValueError("src/dst cache lists must be non-empty and of equal length")
+    for s_, d_ in zip(src_caches, dst_caches):
+        if s_.dtype != d_.dtype or s_.shape[0] != 2 or s_.shape[2:] != d_.shape[2:]:
+            raise ValueError("caches must share dtype and [2, *, kv, bs, D] geometry")
+        if not (s_.is_cuda or s_.is_pinned()) or not (d_.is_cuda or d_.is_pinned()):
+            raise ValueError("caches must be device tensors or pinned host tensors")
+        if not s_.is_contiguous() or not d_.is_contiguous():
+            raise ValueError("caches must be contiguous")
+    _cuda(pairs)
+    _i32(pairs, "pairs")
+    n = len(src_caches)
+    block_bytes = src_caches[0][0, 0].numel() * src_caches[0].element_size()
+    src = (ctypes.c_void_p * n)(*[t.data_ptr() for t in src_caches])
+    dst = (ctypes.c_void_p * n)(*[t.data_ptr() for t in dst_caches])
+    L.check(L.lib().nb_swap_kv_blocks(
+        ctypes.cast(src, ctypes.c_void_p), ctypes.cast(dst, ctypes.c_void_p), n,
+        pairs.data_ptr(), pairs.shape[0], src_caches[0].shape[1], dst_caches[0].shape[1],
+        block_bytes, _stream(pairs)))
+
+
 def device_errors() -> int:
     """Synchronise and return (and clear) the device error word; see
     ``NB_DEVERR_*`` in the header."""

@@ -434,3 +434,37 @@ def test_prefill_every_kernel_version(cuda, version):
     r = subprocess.run([sys.executable, "-c", _PREFILL_CHECK], cwd=root, env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_swap_kv_blocks_round_trip(cuda, dt):
+    """Swap-out to a pinned host cache and swap-in to other device blocks,
+    all layers in one launch each, against needle's per-block copies
+    (runner.py:187-192): cpu[:, dst] = gpu[:, src], then gpu[:, dst] = cpu[:, src]."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(31)
+    L_, N, M, kv, D = 3, 20, 10, 2, 64
+    gpu = [torch.randn(2, N, kv, 16, D, generator=g).to(dt).to(cuda) for _ in range(L_)]
+    cpu = [torch.zeros(2, M, kv, 16, D, dtype=dt).pin_memory() for _ in range(L_)]
+    out_map = {3: 0, 7: 5, 19: 9}
+    ops.swap_kv_blocks(gpu, cpu, torch.tensor(list(out_map.items()), dtype=torch.int32,
+                                               device=cuda))
+    torch.cuda.synchronize()
+    for l_ in range(L_):
+        ref = torch.zeros_like(cpu[l_])
+        for s_, d_ in out_map.items():
+            ref[:, d_] = gpu[l_][:, s_].cpu()
+        assert _bits_equal(cpu[l_], ref)
+    before = [t.clone() for t in gpu]
+    in_map = {0: 11, 5: 2, 9: 19}
+    ops.swap_kv_blocks(cpu, gpu, torch.tensor(list(in_map.items()), dtype=torch.int32,
+                                               device=cuda))
+    torch.cuda.synchronize()
+    for l_ in range(L_):
+        ref = before[l_].cpu()
+        for s_, d_ in in_map.items():
+            ref[:, d_] = cpu[l_][:, s_]
+        assert _bits_equal(gpu[l_], ref)
+    assert ops.device_errors() == 0
+    ops.swap_kv_blocks(gpu, cpu, torch.tensor([[N + 3, 1]], dtype=torch.int32, device=cuda))
+    assert ops.device_errors() & 1        # out-of-range source block flagged, nothing copied
