@@ -454,6 +454,10 @@ def run_model(args):
     steps_left = out_tokens - (1 if prefill else 0)
     W = min(max(3, args.warmup), max(1, steps_left // 4))
     K = min(args.steps, steps_left - W)
+    # capture every decode graph the warm-up and timed steps will use, as a
+    # server does at start-up (no capture inside the timed region)
+    longest = max(len(s.token_ids) for s in seqs)
+    runner.capture_decode_graphs(len(seqs), (longest + W + K + 15) // 16, (longest + 15) // 16)
     for _ in range(W):
         drv.step()
     torch.cuda.synchronize(dev)

@@ -275,6 +275,23 @@ class ModelRunner:
         self._graphs[(B, width)] = g
         return g
 
+    def capture_decode_graphs(self, batch_size: int, max_blocks_per_seq: int,
+                              min_blocks_per_seq: int = 1) -> None:
+        """Capture the decode graphs a batch of ``batch_size`` will use while
+        its block tables grow from ``min_blocks_per_seq`` to
+        ``max_blocks_per_seq`` columns, so that no capture (two eager
+        warm-up forwards plus the capture itself) happens mid-run.  Servers
+        call this at start-up for the batch sizes they serve."""
+        if not self.cuda_graph:
+            return
+        step = self.GRAPH_WIDTH_STEP
+        lo = -(-max(1, min_blocks_per_seq) // step) * step
+        hi = -(-max(1, max_blocks_per_seq) // step) * step
+        with torch.no_grad():
+            for w in range(lo, hi + 1, step):
+                if (batch_size, w) not in self._graphs:
+                    self._capture_decode(batch_size, w)
+
     def release_graphs(self) -> None:
         """Drop captured graphs (required before destroying an NCCL group)."""
         self._graphs.clear()
