@@ -514,7 +514,7 @@ def run_model(args):
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
-    runner.release_graphs()
+    runner.close()
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -217,6 +217,35 @@ NB_API int nb_swap_kv_blocks(const void* const* src_caches, void* const* dst_cac
                              void* stream);
 
 /*
+ * CUDA IPC plumbing for the fused TP all-reduce: export the allocation that
+ * contains dev_ptr (64-byte handle + offset of dev_ptr inside it), map a
+ * peer's handle (the caller adds the offset), unmap.
+ */
+NB_API int nb_ipc_handle(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+NB_API int nb_ipc_open(const void* handle, void** dev_ptr_out);
+NB_API int nb_ipc_close(void* dev_ptr);
+
+/*
+ * Tensor-parallel all-reduce of the row-parallel projection output fused
+ * with the decoder's residual add and RMSNorm, over NVLink peer memory.
+ * Replaces needle/layers/linear.py:92-98 (dist.all_reduce of o_proj /
+ * down_proj) + needle/model/llama.py:67-72 (residual add, RMSNorm).
+ * Every rank passes world-long arrays of peer-mapped pointers (index =
+ * rank): partials[p] = rank p's partial sums [T, hidden]; residuals[p] =
+ * rank p's residual buffer (input and output, updated in place); outs[p] =
+ * rank p's normalised-output buffer; flags[p] = rank p's zero-initialised
+ * flag array of 2*1024*8 uint32.  epochs: this rank's zero-initialised
+ * 1024 uint32 (device).  Every rank computes the same sum in rank order, so
+ * all ranks hold identical bits.  T <= 1024 * world, hidden % 8 == 0 and
+ * <= 8192, bf16/fp16.  All ranks must make the same sequence of calls.
+ */
+NB_API int nb_tp_allreduce_add_rmsnorm(const void* const* partials, void* const* outs,
+                                       void* const* residuals, unsigned* const* flags,
+                                       unsigned* epochs, int rank, int world, const void* weight,
+                                       int num_tokens, int hidden, float eps, int dtype,
+                                       void* stream);
+
+/*
  * SwiGLU activation over a fused gate/up projection: gate_up is [T, 2*I]
  * (gate in columns [0, I), up in [I, 2I)), out[T, I] = silu(gate) * up with
  * the rounding points of needle/model/llama.py:37 (F.silu, then the

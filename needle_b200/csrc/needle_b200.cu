@@ -10,4 +10,5 @@
 #include "norm.cuh"
 #include "act.cuh"
 #include "swap.cuh"
+#include "tp_allreduce.cuh"
 #include "noalloc.cuh"

@@ -4,7 +4,9 @@ Mirrors ``needle/layers/linear.py:21-98``: ``ColumnParallelLinear`` holds
 ``weight[out/tp, in]`` (+ optional bias) and needs no communication;
 ``RowParallelLinear`` holds ``weight[out, in/tp]`` and all-reduces (SUM) its
 output over the tensor-parallel group before adding the bias.  The GEMMs stay
-on torch (cuBLAS); the all-reduce is NCCL through ``torch.distributed``.
+on torch (cuBLAS); the all-reduce is NCCL through ``torch.distributed``, or,
+with a ``TPComm`` attached, the fused all-reduce + residual + RMSNorm kernel
+run by the following ``RMSNorm``.
 """
 from __future__ import annotations
 
@@ -60,7 +62,13 @@ class RowParallelLinear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(out_features)) if bias else None
         nn.init.kaiming_uniform_(self.weight)
 
+    comm = None  # TPComm: defer the all-reduce to the next RMSNorm (fused kernel)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.comm is not None and self.comm.can_fuse(x.shape[0]) and x.dim() == 2:
+            # partial sums into the peer-mapped buffer; the following RMSNorm
+            # all-reduces them together with the residual add and the norm
+            return torch.mm(x, self.weight.t(), out=self.comm.partial[:x.shape[0]])
         out = F.linear(x, self.weight)
         if self.reduce_output and self.tp_size > 1:
             dist.all_reduce(out, op=dist.ReduceOp.SUM, group=tp_group())

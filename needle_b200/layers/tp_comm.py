@@ -1,0 +1,146 @@
+"""Peer-mapped buffers for the fused tensor-parallel all-reduce + residual + RMSNorm.
+
+needle all-reduces the output of every row-parallel projection with NCCL
+(``needle/layers/linear.py:92-98``) and then runs the decoder's residual add
+and RMSNorm (``needle/model/llama.py:67-72``).  ``TPComm`` replaces that pair
+with one kernel (``nb_tp_allreduce_add_rmsnorm``) that reads every rank's
+partial sums over NVLink, adds the residual, normalises and writes the result
+into every rank's buffers.
+
+Each rank allocates one device buffer ``[flags | partial | out | residual]``
+and exports it with CUDA IPC; the handles are exchanged once through
+``torch.distributed`` and every peer's buffer is mapped into this process.
+``RowParallelLinear`` writes its partial GEMM output into ``partial`` and
+``RMSNorm`` recognises that tensor and launches the fused kernel, so the
+sequence of modules (and needle's module API) is unchanged.  All pointers are
+fixed for the life of the object, so the launches can be captured in CUDA
+graphs.  Calls with more tokens than the buffers hold fall back to NCCL.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import _lib as L
+
+_FLAG_BYTES = 2 * 1024 * 8 * 4      # [2 barriers][1024 rows per rank][8 ranks] uint32
+_MAX_ROWS_PER_RANK = 1024
+_MAX_WORLD = 8
+_MAX_HIDDEN = 8192
+_SEGMENT = 2 << 20                  # whole allocator segments: nothing else shares the mapping
+
+
+class TPComm:
+    """One rank's view of the shared all-reduce buffers.
+
+    ``max_tokens`` bounds the rows of one call (decode batch size, or a short
+    prefill); it is clamped to ``1024 * world``.
+    """
+
+    def __init__(self, max_tokens: int, hidden: int, dtype: torch.dtype, device,
+                 group=None):
+        if not (dist.is_available() and dist.is_initialized()):
+            raise RuntimeError("TPComm needs an initialised torch.distributed process group")
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise TypeError("the fused TP all-reduce supports bf16 and fp16")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _MAX_WORLD:
+            raise ValueError(f"world size {self.world} exceeds {_MAX_WORLD}")
+        if hidden % 8 or hidden > _MAX_HIDDEN:
+            raise ValueError(f"hidden {hidden} must be a multiple of 8 up to {_MAX_HIDDEN}")
+        self.hidden, self.dtype = hidden, dtype
+        self.device = torch.device(device)
+        self.max_tokens = min(int(max_tokens), _MAX_ROWS_PER_RANK * self.world)
+        esz = torch.empty((), dtype=dtype).element_size()
+        n = -(-self.max_tokens * hidden * esz // 256) * 256
+        total = -(-(_FLAG_BYTES + 3 * n) // _SEGMENT) * _SEGMENT
+        self._buf = torch.zeros(total, dtype=torch.uint8, device=self.device)
+        self.epochs = torch.zeros(_MAX_ROWS_PER_RANK, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)  # zeroed flags before any peer can see them
+
+        def view(off):
+            return self._buf[off:off + self.max_tokens * hidden * esz].view(dtype).view(
+                self.max_tokens, hidden)
+        self.partial = view(_FLAG_BYTES)
+        self.out = view(_FLAG_BYTES + n)
+        self.residual = view(_FLAG_BYTES + 2 * n)
+
+        lib = L.lib()
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_uint64(0)
+        L.check(lib.nb_ipc_handle(self._buf.data_ptr(), ctypes.addressof(handle),
+                                  ctypes.addressof(offset)))
+        entries: List[Optional[tuple]] = [None] * self.world
+        dist.all_gather_object(entries, (bytes(handle), offset.value), group=group)
+        self._opened: List[int] = []
+        bases = []
+        for p, (h, off) in enumerate(entries):
+            if p == self.rank:
+                bases.append(self._buf.data_ptr())
+                continue
+            hb = (ctypes.c_char * 64).from_buffer_copy(h)
+            ptr = ctypes.c_void_p(0)
+            L.check(lib.nb_ipc_open(ctypes.addressof(hb), ctypes.addressof(ptr)))
+            self._opened.append(ptr.value)
+            bases.append(ptr.value + off)
+        W = self.world
+        self._flags = (ctypes.c_void_p * W)(*[b for b in bases])
+        self._parts = (ctypes.c_void_p * W)(*[b + _FLAG_BYTES for b in bases])
+        self._outs = (ctypes.c_void_p * W)(*[b + _FLAG_BYTES + n for b in bases])
+        self._ress = (ctypes.c_void_p * W)(*[b + _FLAG_BYTES + 2 * n for b in bases])
+        self._epochs = ctypes.cast(ctypes.c_void_p(self.epochs.data_ptr()),
+                                   ctypes.POINTER(ctypes.c_uint))
+        dist.barrier(group=group)  # every rank has mapped every buffer
+
+    def can_fuse(self, num_tokens: int) -> bool:
+        return 0 < num_tokens <= self.max_tokens
+
+    def is_partial(self, x: torch.Tensor) -> bool:
+        """True if ``x`` is the partial-sum view that ``RowParallelLinear``
+        returned for the fused path."""
+        return x.data_ptr() == self.partial.data_ptr() and x.dim() == 2
+
+    def allreduce_add_rmsnorm(self, num_tokens: int, residual: torch.Tensor,
+                              weight: torch.Tensor, eps: float):
+        """All-reduce ``partial[:T]`` over the group, add ``residual``, RMSNorm
+        with ``weight``.  Returns ``(normed, new_residual)`` as views of this
+        object's ``out`` and ``residual`` buffers (identical on every rank)."""
+        T = num_tokens
+        res = self.residual[:T]
+        if residual.data_ptr() != res.data_ptr():
+            res.copy_(residual)
+        if weight.dtype != self.dtype or not weight.is_contiguous():
+            raise TypeError("weight must be contiguous and of the buffers' dtype")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        L.check(L.lib().nb_tp_allreduce_add_rmsnorm(
+            ctypes.cast(self._parts, ctypes.c_void_p), ctypes.cast(self._outs, ctypes.c_void_p),
+            ctypes.cast(self._ress, ctypes.c_void_p), ctypes.cast(self._flags, ctypes.c_void_p),
+            self._epochs, self.rank, self.world, weight.data_ptr(), T, self.hidden, float(eps),
+            2 if self.dtype == torch.bfloat16 else 1, stream))
+        return self.out[:T], res
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after all work that uses them finished)."""
+        if self._opened:
+            torch.cuda.synchronize(self.device)
+            lib = L.lib()
+            for p in self._opened:
+                lib.nb_ipc_close(p)
+            self._opened = []
+
+
+def attach(model: torch.nn.Module, comm: Optional[TPComm]) -> None:
+    """Point every ``RowParallelLinear`` without bias and every ``RMSNorm`` of
+    ``model`` at ``comm`` (``None`` detaches)."""
+    from .linear import RowParallelLinear
+    from .norm import RMSNorm
+    for m in model.modules():
+        if isinstance(m, RowParallelLinear) and m.bias is None and m.reduce_output:
+            m.comm = comm
+        elif isinstance(m, RMSNorm):
+            m.comm = comm

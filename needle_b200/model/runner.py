@@ -98,7 +98,7 @@ class ModelRunner:
 
     def __init__(self, model_config: ModelConfig, block_size: int = 16, dtype: str = "bfloat16",
                  device: str = "cuda", tensor_parallel_size: int = 1, tp_rank: int = 0,
-                 cuda_graph: bool = True, fuse: bool = True):
+                 cuda_graph: bool = True, fuse: bool = True, tp_fused_tokens: int = 1024):
         self.model_config = model_config
         self.block_size = block_size
         self.device = torch.device(device)
@@ -127,6 +127,16 @@ class ModelRunner:
         if tensor_parallel_size > 1 and os.environ.get("NB_TP_GRAPH", "1") == "0":
             cuda_graph = False
         self.cuda_graph = cuda_graph
+        # Under TP with bf16/fp16, calls of up to tp_fused_tokens rows run the
+        # row-parallel all-reduce fused with the residual add and RMSNorm over
+        # NVLink peer memory; larger calls (long prefills) use NCCL.
+        # NB_TP_FUSED=0 keeps NCCL everywhere.
+        self.tp_comm = None
+        if (tensor_parallel_size > 1 and self.dtype in (torch.bfloat16, torch.float16)
+                and tp_fused_tokens > 0 and os.environ.get("NB_TP_FUSED", "1") != "0"):
+            from ..layers.tp_comm import TPComm, attach
+            self.tp_comm = TPComm(tp_fused_tokens, cfg.hidden_size, self.dtype, self.device)
+            attach(self.model, self.tp_comm)
         self.padding_block = 0
         self._graphs: Dict[tuple, _DecodeGraph] = {}
         self._graph_pool = None
@@ -296,6 +306,16 @@ class ModelRunner:
         """Drop captured graphs (required before destroying an NCCL group)."""
         self._graphs.clear()
         self._graph_pool = None
+
+    def close(self) -> None:
+        """Release graphs and unmap the peers' all-reduce buffers; call on
+        every rank before destroying the process group."""
+        self.release_graphs()
+        if self.tp_comm is not None:
+            from ..layers.tp_comm import attach
+            attach(self.model, None)
+            self.tp_comm.close()
+            self.tp_comm = None
 
     def _swap_kv_blocks(self, mapping: dict, direction: str) -> None:
         """Copy whole blocks between the device and pinned host caches

@@ -100,3 +100,79 @@ def test_per_rank_head_counts_match_needle(H, KV, tp, hl, kvl):
         a = Attention(cfg, 0, tp_size=tp, tp_rank=0)
     assert (a.num_heads, a.num_kv_heads) == (hl, kvl)
     assert a.q_proj.weight.shape[0] == hl * 64 and a.k_proj.weight.shape[0] == kvl * 64
+
+
+class _HostComm:
+    """Stand-in for ``TPComm`` with the same interface, reducing with gloo on
+    the CPU: checks that ``RowParallelLinear`` hands its partial sum to the
+    following ``RMSNorm`` and that the norm receives the residual."""
+
+    def __init__(self, max_tokens, hidden):
+        self.partial = torch.zeros(max_tokens, hidden)
+        self.residual = torch.zeros(max_tokens, hidden)
+        self.max_tokens = max_tokens
+        self.calls = 0
+
+    def can_fuse(self, n):
+        return 0 < n <= self.max_tokens
+
+    def is_partial(self, x):
+        return x.data_ptr() == self.partial.data_ptr()
+
+    def allreduce_add_rmsnorm(self, T, residual, weight, eps):
+        from oracle.needle_oracle import add_rms_norm
+        self.calls += 1
+        s = self.partial[:T].clone()
+        dist.all_reduce(s)
+        y, h = add_rms_norm(s, residual, weight, eps)
+        self.residual[:T].copy_(h)
+        return y, self.residual[:T]
+
+
+def _fused_worker(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from needle_b200.layers.norm import RMSNorm
+        from needle_b200.layers.tp_comm import attach
+        from oracle.needle_oracle import add_rms_norm
+        g = torch.Generator().manual_seed(0)
+        hid, T = 64, 5
+        Wo = torch.randn(hid, hid, generator=g)
+        attn = torch.randn(T, hid, generator=g)
+        res = torch.randn(T, hid, generator=g)
+        nw = 1 + 0.1 * torch.randn(hid, generator=g)
+        ref_y, ref_h = add_rms_norm(F.linear(attn, Wo), res, nw, 1e-6)
+        blk = torch.nn.ModuleDict({"o": RowParallelLinear(hid, hid, tp_size=world, tp_rank=rank),
+                                   "norm": RMSNorm(hid, eps=1e-6)})
+        comm = _HostComm(16, hid)
+        attach(blk, comm)
+        with torch.no_grad():
+            blk["o"].weight.copy_(shard_for_rank("self_attn.o_proj.weight", Wo, world, rank))
+            blk["norm"].weight.copy_(nw)
+            part = blk["o"](attn.narrow(1, rank * hid // world, hid // world))
+            assert comm.is_partial(part)
+            y, h = blk["norm"](part, res)
+        attach(blk, None)
+        assert blk["o"].comm is None and blk["norm"].comm is None
+        q.put((rank, (comm.calls, float((y - ref_y).abs().max()), float((h - ref_h).abs().max()))))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
+def test_deferred_allreduce_reaches_norm_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 28500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert isinstance(res[r], tuple), res[r]
+        calls, ey, eh = res[r]
+        assert calls == 1 and ey < 1e-4 and eh < 1e-4, res
