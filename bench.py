@@ -497,7 +497,10 @@ def run_model(args):
                        "prompt_tokens": sum(len(p) for p in prompts) if prefill else None,
                        "ctx_at_first_timed_step": round(ctx_sum / B, 1),
                        "prefill_ms": round(t_prefill_ms, 1) if t_prefill_ms else None,
-                       "parallelism": f"tp{ws}"},
+                       "parallelism": f"tp{ws}",
+                       "allreduce": (None if ws == 1 else
+                                     "fused all-reduce+residual+RMSNorm over NVLink peer memory"
+                                     if runner.tp_comm is not None else "NCCL")},
             "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + KV per rank)",
                          "achieved": round(step_bytes * K / (t_ms / 1e3) / 1e9, 1),
                          "peak": peak, "unit": "GB/s",

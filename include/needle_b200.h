@@ -230,20 +230,22 @@ NB_API int nb_ipc_close(void* dev_ptr);
  * with the decoder's residual add and RMSNorm, over NVLink peer memory.
  * Replaces needle/layers/linear.py:92-98 (dist.all_reduce of o_proj /
  * down_proj) + needle/model/llama.py:67-72 (residual add, RMSNorm).
- * Every rank passes world-long arrays of peer-mapped pointers (index =
- * rank): partials[p] = rank p's partial sums [T, hidden]; residuals[p] =
- * rank p's residual buffer (input and output, updated in place); outs[p] =
- * rank p's normalised-output buffer; flags[p] = rank p's zero-initialised
- * flag array of 2*1024*8 uint32.  epochs: this rank's zero-initialised
- * 1024 uint32 (device).  Every rank computes the same sum in rank order, so
- * all ranks hold identical bits.  T <= 1024 * world, hidden % 8 == 0 and
- * <= 8192, bf16/fp16.  All ranks must make the same sequence of calls.
+ * partial: this rank's partial sums [T, hidden]; residual: the residual
+ * [T, hidden], updated in place; out: the normalised rows [T, hidden] (all
+ * three local).  recv / gather: world-long arrays of peer-mapped pointers
+ * (index = rank) to each rank's receive slots [2][world][slot_rows][hidden]
+ * and gather slots [2][world][slot_rows][2][hidden], filled with 0xFF bytes
+ * before first use.  epochs: this rank's zero-initialised 2048 uint32
+ * (device).  Every owner sums the partials in rank order, so all ranks hold
+ * identical bits.  ceil(T / world) <= min(1024, slot_rows), hidden % 8 == 0
+ * and <= 8192, bf16/fp16, 16-byte aligned buffers.  All ranks must make the
+ * same sequence of calls.
  */
-NB_API int nb_tp_allreduce_add_rmsnorm(const void* const* partials, void* const* outs,
-                                       void* const* residuals, unsigned* const* flags,
-                                       unsigned* epochs, int rank, int world, const void* weight,
-                                       int num_tokens, int hidden, float eps, int dtype,
-                                       void* stream);
+NB_API int nb_tp_allreduce_add_rmsnorm(const void* partial, void* const* recv,
+                                       void* const* gather, int slot_rows, void* out,
+                                       void* residual, unsigned* epochs, int rank, int world,
+                                       const void* weight, int num_tokens, int hidden, float eps,
+                                       int dtype, void* stream);
 
 /*
  * SwiGLU activation over a fused gate/up projection: gate_up is [T, 2*I]

@@ -4,24 +4,33 @@
 // sum on every rank (needle/layers/linear.py:92-98 all-reduces it with NCCL)
 // and the decoder then adds the residual and normalises
 // (needle/model/llama.py:67-72).  This kernel does all three in one launch
-// over NVLink peer memory:
-//   * rank r owns rows [r*R, r*R+R) (R = ceil(T / world)); CTA b of every
-//     rank handles row r*R + b of its own rank;
-//   * barrier 1: CTA b announces to every peer that this rank's partial is
-//     complete (its GEMM finished before this kernel started), then waits
-//     until every peer's CTA b has done the same;
-//   * it sums the row over all ranks' partial buffers in rank order 0..W-1
-//     (the same order on every rank, so every rank computes identical
-//     bits), rounds the sum to the storage type (the all-reduced tensor),
-//     adds the residual, normalises, and stores the new residual row and the
-//     normalised row into every rank's buffers (plain peer stores);
-//   * barrier 2: CTA b announces its stores are done and waits for every
-//     peer's CTA b.  When all CTAs of a rank have passed it, every peer has
-//     written its rows into this rank's buffers.
-// Flags hold per-CTA epochs that each rank keeps in its own memory and bumps
-// on every call, so the same launch can be replayed from a CUDA graph.
+// over NVLink peer memory, as a reduce-scatter followed by an all-gather,
+// with no flags and no fences: the data is its own arrival signal.
+//
+//   * Every receive buffer starts filled with a sentinel bit pattern (0xFFFF
+//     in every 16-bit lane, a NaN) that valid data never holds: senders
+//     rewrite that one NaN pattern to another NaN (0x7FFF) before storing.
+//     A reader polls a 16-byte vector until none of its lanes is the
+//     sentinel, consumes it, and writes the sentinel back.
+//   * Rank q owns rows [q*R, q*R+R) (R = ceil(T / world)).  CTA b of every
+//     rank handles row index b: it pushes its partial of row q*R+b into
+//     owner q's receive slot [sender][b]; as owner it waits for all world
+//     slots of its row b, sums them in rank order 0..W-1 (the same order on
+//     every owner: identical bits everywhere), rounds to the storage type
+//     (the all-reduced tensor), adds the residual, normalises, and pushes
+//     the new residual row and the normalised row into every rank's gather
+//     slot [owner][b]; finally it waits for the world gather slots of index
+//     b and copies them into this rank's residual and output rows.
+//   * When the GPU holds two CTAs per row index at once, the second
+//     receives the gathered normalised rows while the first receives the
+//     residual rows, so both receive batches are in flight together.
+//   * Receive and gather buffers are double-buffered by the parity of a
+//     per-row-index call counter (epochs[role][b]).  A sender writes a buffer half
+//     again two calls later; by then its previous call has received this
+//     rank's results of the call in between, which this rank sent after it
+//     had consumed (and reset) the half being rewritten.
 // Waits are bounded; on a timeout the kernel records NB_DEVERR_TIMEOUT and
-// returns.  Only plain loads and stores cross NVLink.
+// returns.  Only plain 16-byte loads and stores cross NVLink.
 #pragma once
 #include <algorithm>
 #include <cstring>
@@ -31,139 +40,229 @@
 namespace nb {
 
 constexpr int kArMaxRanks = 8;
-constexpr int kArMaxCtas = 1024;  // rows per rank
+constexpr int kArMaxRows = 1024;  // rows per rank (row indices b); epochs hold 2 x this
 
 struct ArPeers {
-  const void* part[kArMaxRanks];  // each rank's partial-sum buffer [T, hidden]
-  void* out[kArMaxRanks];         // each rank's normalised-output buffer
-  void* res[kArMaxRanks];         // each rank's residual buffer (read and updated)
-  unsigned* flags[kArMaxRanks];   // each rank's flags [2][kArMaxCtas][kArMaxRanks]
+  void* recv[kArMaxRanks];    // each rank's receive slots [2][world][slot_rows][hidden]
+  void* gather[kArMaxRanks];  // each rank's gather slots [2][world][slot_rows][2][hidden]
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+constexpr unsigned kArSentinel = 0xFFFFFFFFu;
+
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
-// Signal this CTA's arrival to every rank, then wait for every rank's CTA b.
-// Returns false if a peer did not arrive within kWaitLimitNs.
-__device__ __forceinline__ bool ar_barrier(const ArPeers& P, int which, int b, int rank, int world,
-                                           unsigned e) {
-  bool ok = true;
-  if (threadIdx.x < world) {
-    __threadfence_system();
-    st_release_sys(P.flags[threadIdx.x] + ((size_t)which * kArMaxCtas + b) * kArMaxRanks + rank, e);
-  }
-  if (threadIdx.x < world) {
-    const unsigned* f =
-        P.flags[rank] + ((size_t)which * kArMaxCtas + b) * kArMaxRanks + threadIdx.x;
-    if ((int)(ld_acquire_sys(f) - e) < 0) {
-      const unsigned long long t0 = globaltimer();
-      while ((int)(ld_acquire_sys(f) - e) < 0) {
-        if (globaltimer() - t0 > kWaitLimitNs) { ok = false; break; }
-      }
+__device__ __forceinline__ bool lane_is_sentinel(unsigned w) {
+  return (w & 0xFFFFu) == 0xFFFFu || (w >> 16) == 0xFFFFu;
+}
+__device__ __forceinline__ bool arrived(const uint4& v) {
+  return !(lane_is_sentinel(v.x) || lane_is_sentinel(v.y) || lane_is_sentinel(v.z) ||
+           lane_is_sentinel(v.w));
+}
+// The sentinel NaN becomes another NaN, so data never reads as "not arrived".
+__device__ __forceinline__ unsigned canon_word(unsigned w) {
+  if ((w & 0xFFFFu) == 0xFFFFu) w = (w & 0xFFFF0000u) | 0x7FFFu;
+  if ((w >> 16) == 0xFFFFu) w = (w & 0x0000FFFFu) | 0x7FFF0000u;
+  return w;
+}
+__device__ __forceinline__ uint4 canon(uint4 v) {
+  return make_uint4(canon_word(v.x), canon_word(v.y), canon_word(v.z), canon_word(v.w));
+}
+
+// Re-poll a 16-byte vector that had not arrived at the first look, until it
+// arrives; gives up (dead = true) after kWaitLimitNs, or at once if an
+// earlier wait of this thread already gave up.
+__device__ __forceinline__ uint4 wait_vec_slow(const void* p, bool* dead) {
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (*dead) return v;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    v = ld_volatile_v4(p);
+    if (arrived(v)) return v;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *dead = true;
+      return v;
     }
   }
-  return __syncthreads_and(ok) != 0;
+}
+
+// N vectors at base + i * stride (elements of 16-bit T), i < n: all loads in
+// flight at once (one memory round trip when everything has arrived), then
+// the stragglers one by one.  Each slot is reset to the sentinel after it is
+// read.
+template <int N, typename T>
+__device__ __forceinline__ void gather_vecs(T* base, int64_t stride, int n, uint4 (&v)[N],
+                                            bool& dead) {
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < n) v[i] = ld_volatile_v4(base + i * stride);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < n && !arrived(v[i])) v[i] = wait_vec_slow(base + i * stride, &dead);
+  const uint4 sentinel = make_uint4(kArSentinel, kArSentinel, kArSentinel, kArSentinel);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < n) *reinterpret_cast<uint4*>(base + i * stride) = sentinel;
 }
 
 template <typename T, int VEC>
 __global__ void __launch_bounds__(1024)
-    tp_allreduce_add_rmsnorm_kernel(const __grid_constant__ ArPeers P, unsigned* __restrict__ epochs,
-                                    int rank, int world, const T* __restrict__ weight, int rows,
-                                    int hidden, float eps) {
+    tp_allreduce_add_rmsnorm_kernel(const __grid_constant__ ArPeers P, const T* __restrict__ partial,
+                                    T* __restrict__ out, T* __restrict__ res, int slot_rows,
+                                    unsigned* __restrict__ epochs, int rank, int world,
+                                    const T* __restrict__ weight, int rows, int hidden, float eps,
+                                    int split) {
+  static_assert(VEC * sizeof(T) == 16, "one 16-byte vector per thread");
   __shared__ float red[32];
   __shared__ unsigned s_e;
   const int per = (rows + world - 1) / world;
   const int nvec = hidden / VEC;
   const bool mine = threadIdx.x < nvec;  // one vector per thread (hidden <= 1024 * VEC)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t col = (int64_t)threadIdx.x * VEC;
+  const int64_t slot = (int64_t)slot_rows * hidden;  // elements per sender slot
+  // With split, two CTAs per row index b: role 0 pushes, reduces the rows it
+  // owns and receives the gathered residual rows; role 1 receives the
+  // gathered normalised rows, so that both receive batches are in flight
+  // together.  Without split (more row indices than resident CTA pairs),
+  // role 0 receives both.
+  const int G = split ? gridDim.x >> 1 : gridDim.x;
+  const int role = split && blockIdx.x >= G;
+  unsigned* ep = epochs + role * kArMaxRows;  // per-role call counters
+  bool dead = false;
+  uint4 v[kArMaxRanks];
+  uint4 w4 = make_uint4(0, 0, 0, 0);
+  if (role == 0 && mine) w4 = __ldg(reinterpret_cast<const uint4*>(weight + col));
   // The grid is at most what fits on the GPU at once (every CTA resident), so
   // a CTA waiting on a peer never blocks the CTA that the peer waits for.
-  for (int b = blockIdx.x; b < per; b += gridDim.x) {
-    if (threadIdx.x == 0) s_e = epochs[b] + 1;
-    __syncthreads();
-    const unsigned e = s_e;
-    if (!ar_barrier(P, 0, b, rank, world, e)) {
+  for (int b = blockIdx.x - role * G; b < per; b += G) {
+    if (threadIdx.x == 0) s_e = ep[b];
+    // owners q with a row at index b: q*per+b < rows
+    const int nq = min(world, (rows - 1 - b) / per + 1);
+    if (role == 0) {
+      // 1. reduce-scatter: row q*per+b of this rank's partial -> owner q, slot [rank][b]
+      //    (the partial loads overlap the call-counter load)
+      if (mine) {
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < nq)
+            v[q] = *reinterpret_cast<const uint4*>(partial + (int64_t)(q * per + b) * hidden + col);
+      }
+      __syncthreads();
+      const int par = s_e & 1;
+      if (mine) {
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < nq)
+            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(P.recv[q]) +
+                                      ((int64_t)par * world + rank) * slot + (int64_t)b * hidden +
+                                      col) = canon(v[q]);
+      }
+      // 2. owner of row rank*per+b: sum the world slots, residual, RMSNorm, all-gather
+      const int row = rank * per + b;
+      if (row < rows) {  // uniform over the CTA
+        float ss = 0.f;
+        T hv[VEC];
+        if (mine) {
+          T* rb = reinterpret_cast<T*>(P.recv[rank]) + (int64_t)par * world * slot +
+                  (int64_t)b * hidden + col;
+          T rv[VEC];
+          *reinterpret_cast<uint4*>(rv) =
+              *reinterpret_cast<const uint4*>(res + (int64_t)row * hidden + col);
+          float acc[VEC];
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
+          gather_vecs<kArMaxRanks>(rb, slot, world, v, dead);  // slots reset for two calls later
+#pragma unroll
+          for (int p = 0; p < kArMaxRanks; ++p) {  // fixed rank order: identical bits everywhere
+            if (p < world) {
+              const T* x = reinterpret_cast<const T*>(&v[p]);
+#pragma unroll
+              for (int k = 0; k < VEC; ++k) acc[k] = __fadd_rn(acc[k], Dt<T>::to_f(x[k]));
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) {
+            // all-reduced value rounded to the storage type, then residual + it
+            const float sum = Dt<T>::round(acc[k]);
+            hv[k] = Dt<T>::from_f(__fadd_rn(Dt<T>::to_f(rv[k]), sum));
+            const float f = Dt<T>::to_f(hv[k]);
+            ss = __fadd_rn(ss, __fmul_rn(f, f));
+          }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (warp == 0) {
+          float x = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+          x = warp_sum(x);
+          if (lane == 0) red[0] = x;
+        }
+        __syncthreads();
+        if (mine) {
+          const float var = __fdiv_rn(red[0], (float)hidden);
+          const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+          const T* wv = reinterpret_cast<const T*>(&w4);
+          T ov[VEC];
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) {
+            const float xn = Dt<T>::round(__fmul_rn(Dt<T>::to_f(hv[k]), r));
+            ov[k] = Dt<T>::from_f(__fmul_rn(Dt<T>::to_f(wv[k]), xn));
+          }
+          const uint4 h4 = canon(*reinterpret_cast<uint4*>(hv));
+          const uint4 o4 = canon(*reinterpret_cast<uint4*>(ov));
+          const int64_t g =
+              ((int64_t)par * world + rank) * 2 * slot + (int64_t)b * 2 * hidden + col;
+#pragma unroll
+          for (int p = 0; p < kArMaxRanks; ++p) {
+            if (p < world) {
+              T* gp = reinterpret_cast<T*>(P.gather[p]) + g;
+              *reinterpret_cast<uint4*>(gp) = h4;
+              *reinterpret_cast<uint4*>(gp + hidden) = o4;
+            }
+          }
+        }
+      }
+      // 3. all-gather receive, residual rows q*per+b from their owners q
+      if (mine) {
+        T* gb = reinterpret_cast<T*>(P.gather[rank]) + (int64_t)par * world * 2 * slot +
+                (int64_t)b * 2 * hidden + col;
+        gather_vecs<kArMaxRanks>(gb, 2 * slot, nq, v, dead);
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < nq) *reinterpret_cast<uint4*>(res + (int64_t)(q * per + b) * hidden + col) = v[q];
+        if (!split) {
+          gather_vecs<kArMaxRanks>(gb + hidden, 2 * slot, nq, v, dead);
+#pragma unroll
+          for (int q = 0; q < kArMaxRanks; ++q)
+            if (q < nq)
+              *reinterpret_cast<uint4*>(out + (int64_t)(q * per + b) * hidden + col) = v[q];
+        }
+      }
+    } else {
+      __syncthreads();
+      const int par = s_e & 1;
+      // 3'. all-gather receive, normalised rows q*per+b from their owners q
+      if (mine) {
+        T* gb = reinterpret_cast<T*>(P.gather[rank]) + (int64_t)par * world * 2 * slot +
+                (int64_t)b * 2 * hidden + hidden + col;
+        gather_vecs<kArMaxRanks>(gb, 2 * slot, nq, v, dead);
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (q < nq) *reinterpret_cast<uint4*>(out + (int64_t)(q * per + b) * hidden + col) = v[q];
+      }
+    }
+    if (__syncthreads_or(dead)) {
       if (threadIdx.x == 0) set_error(kErrTimeout);
       return;
     }
-    const int row = rank * per + b;
-    if (row < rows) {  // uniform over the CTA
-      const int64_t off = (int64_t)row * hidden + threadIdx.x * VEC;
-      float ss = 0.f;
-      T hv[VEC];
-      if (mine) {
-        // all ranks' vectors in flight at once, then summed in rank order
-        uint4 raw[kArMaxRanks];
-#pragma unroll
-        for (int p = 0; p < kArMaxRanks; ++p)
-          if (p < world)
-            raw[p] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.part[p]) + off);
-        T rv[VEC];
-        *reinterpret_cast<uint4*>(rv) =
-            *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(P.res[rank]) + off);
-        float acc[VEC];
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
-#pragma unroll
-        for (int p = 0; p < kArMaxRanks; ++p) {
-          if (p < world) {
-            const T* v = reinterpret_cast<const T*>(&raw[p]);
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) acc[k] = __fadd_rn(acc[k], Dt<T>::to_f(v[k]));
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-          // all-reduced value rounded to the storage type, then residual + it
-          const float sum = Dt<T>::round(acc[k]);
-          hv[k] = Dt<T>::from_f(__fadd_rn(Dt<T>::to_f(rv[k]), sum));
-          const float f = Dt<T>::to_f(hv[k]);
-          ss = __fadd_rn(ss, __fmul_rn(f, f));
-        }
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) red[warp] = ss;
-      __syncthreads();
-      if (warp == 0) {
-        float v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
-        v = warp_sum(v);
-        if (lane == 0) red[0] = v;
-      }
-      __syncthreads();
-      if (mine) {
-        const float var = __fdiv_rn(red[0], (float)hidden);
-        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        T wv[VEC], ov[VEC];
-        *reinterpret_cast<uint4*>(wv) =
-            __ldg(reinterpret_cast<const uint4*>(weight + threadIdx.x * VEC));
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-          const float xn = Dt<T>::round(__fmul_rn(Dt<T>::to_f(hv[k]), r));
-          ov[k] = Dt<T>::from_f(__fmul_rn(Dt<T>::to_f(wv[k]), xn));
-        }
-        const uint4 h4 = *reinterpret_cast<uint4*>(hv), o4 = *reinterpret_cast<uint4*>(ov);
-#pragma unroll
-        for (int p = 0; p < kArMaxRanks; ++p) {
-          if (p < world) {
-            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(P.res[p]) + off) = h4;
-            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(P.out[p]) + off) = o4;
-          }
-        }
-        __threadfence_system();  // this thread's peer stores before the CTA's release
-      }
-    }
-    __syncthreads();
-    if (!ar_barrier(P, 1, b, rank, world, e)) {
-      if (threadIdx.x == 0) set_error(kErrTimeout);
-      return;
-    }
-    if (threadIdx.x == 0) epochs[b] = e;
+    if (threadIdx.x == 0) ep[b] = s_e + 1;
   }
 }
 
@@ -217,49 +316,55 @@ int nb_ipc_close(void* dev_ptr) {
   return NB_OK;
 }
 
-int nb_tp_allreduce_add_rmsnorm(const void* const* partials, void* const* outs,
-                                void* const* residuals, unsigned* const* flags,
-                                unsigned* epochs, int rank, int world, const void* weight,
-                                int num_tokens, int hidden, float eps, int dtype, void* stream) {
+int nb_tp_allreduce_add_rmsnorm(const void* partial, void* const* recv, void* const* gather,
+                                int slot_rows, void* out, void* residual, unsigned* epochs,
+                                int rank, int world, const void* weight, int num_tokens,
+                                int hidden, float eps, int dtype, void* stream) {
   using namespace nbh;
   if (!valid_dtype(dtype) || dtype == NB_DTYPE_F32)
     return fail(NB_ERR_UNSUPPORTED, "fused TP all-reduce supports bf16/fp16");
-  if (!partials || !outs || !residuals || !flags || !epochs || !weight)
+  if (!partial || !recv || !gather || !out || !residual || !epochs || !weight)
     return fail(NB_ERR_INVALID_ARG, "null pointer argument");
   if (world < 1 || world > nb::kArMaxRanks || rank < 0 || rank >= world)
     return fail(NB_ERR_INVALID_ARG, "rank %d / world %d out of range", rank, world);
   if (num_tokens < 0 || hidden <= 0 || hidden % 8 || hidden > 1024 * 8)
     return fail(NB_ERR_UNSUPPORTED, "hidden must be a multiple of 8 up to 8192");
   const int per = (num_tokens + world - 1) / world;
-  if (per > nb::kArMaxCtas)
-    return fail(NB_ERR_UNSUPPORTED, "%d rows per rank exceed %d", per, nb::kArMaxCtas);
+  if (per > nb::kArMaxRows)
+    return fail(NB_ERR_UNSUPPORTED, "%d rows per rank exceed %d", per, nb::kArMaxRows);
+  if (per > slot_rows)
+    return fail(NB_ERR_INVALID_ARG, "%d rows per rank exceed the %d slot rows", per, slot_rows);
   if (num_tokens == 0) return NB_OK;
+  if ((uintptr_t)weight % 16 || (uintptr_t)partial % 16 || (uintptr_t)out % 16 ||
+      (uintptr_t)residual % 16)
+    return fail(NB_ERR_INVALID_ARG, "weight, partial, out and residual must be 16-byte aligned");
   nb::ArPeers P;
   for (int p = 0; p < world; ++p) {
-    if (!partials[p] || !outs[p] || !residuals[p] || !flags[p])
-      return fail(NB_ERR_INVALID_ARG, "rank %d: null buffer", p);
-    P.part[p] = partials[p];
-    P.out[p] = outs[p];
-    P.res[p] = residuals[p];
-    P.flags[p] = flags[p];
+    if (!recv[p] || !gather[p]) return fail(NB_ERR_INVALID_ARG, "rank %d: null buffer", p);
+    if ((uintptr_t)recv[p] % 16 || (uintptr_t)gather[p] % 16)
+      return fail(NB_ERR_INVALID_ARG, "rank %d: buffers must be 16-byte aligned", p);
+    P.recv[p] = recv[p];
+    P.gather[p] = gather[p];
   }
-  if ((uintptr_t)weight % 16) return fail(NB_ERR_INVALID_ARG, "weight must be 16-byte aligned");
   const int threads = std::max(32, ((hidden / 8 + 31) / 32) * 32);
   cudaStream_t st = (cudaStream_t)stream;
-  auto launch = [&](auto kern, const auto* w) {
+  auto launch = [&](auto kern, auto* type_tag) {
+    using T = std::remove_pointer_t<decltype(type_tag)>;
     // at most one resident wave: every CTA runs concurrently with its peers
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, 0) != cudaSuccess ||
         occ < 1)
       return fail(NB_ERR_CUDA, "occupancy query failed");
-    const int grid = std::min(per, occ * num_sms());
-    kern<<<grid, threads, 0, st>>>(P, epochs, rank, world, w, num_tokens, hidden, eps);
+    const int cap = occ * num_sms();
+    const int split = 2 * per <= cap;
+    const int grid = split ? 2 * per : std::min(per, cap);
+    kern<<<grid, threads, 0, st>>>(P, (const T*)partial, (T*)out, (T*)residual, slot_rows, epochs,
+                                   rank, world, (const T*)weight, num_tokens, hidden, eps, split);
     return check_launch("tp_allreduce_add_rmsnorm");
   };
   if (dtype == NB_DTYPE_BF16)
-    return launch(nb::tp_allreduce_add_rmsnorm_kernel<__nv_bfloat16, 8>,
-                  (const __nv_bfloat16*)weight);
-  return launch(nb::tp_allreduce_add_rmsnorm_kernel<__half, 8>, (const __half*)weight);
+    return launch(nb::tp_allreduce_add_rmsnorm_kernel<__nv_bfloat16, 8>, (__nv_bfloat16*)nullptr);
+  return launch(nb::tp_allreduce_add_rmsnorm_kernel<__half, 8>, (__half*)nullptr);
 }
 
 }  // extern "C"

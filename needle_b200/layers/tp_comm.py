@@ -3,18 +3,19 @@
 needle all-reduces the output of every row-parallel projection with NCCL
 (``needle/layers/linear.py:92-98``) and then runs the decoder's residual add
 and RMSNorm (``needle/model/llama.py:67-72``).  ``TPComm`` replaces that pair
-with one kernel (``nb_tp_allreduce_add_rmsnorm``) that reads every rank's
-partial sums over NVLink, adds the residual, normalises and writes the result
-into every rank's buffers.
+with one kernel (``nb_tp_allreduce_add_rmsnorm``): every rank pushes each row
+of its partial sums to the rank that owns the row over NVLink, the owner sums
+them, adds the residual, normalises and pushes the result to every rank.
 
-Each rank allocates one device buffer ``[flags | partial | out | residual]``
-and exports it with CUDA IPC; the handles are exchanged once through
-``torch.distributed`` and every peer's buffer is mapped into this process.
-``RowParallelLinear`` writes its partial GEMM output into ``partial`` and
-``RMSNorm`` recognises that tensor and launches the fused kernel, so the
-sequence of modules (and needle's module API) is unchanged.  All pointers are
-fixed for the life of the object, so the launches can be captured in CUDA
-graphs.  Calls with more tokens than the buffers hold fall back to NCCL.
+Each rank allocates one device buffer of receive and gather slots (filled
+with the kernel's sentinel, 0xFF bytes) and exports it with CUDA IPC; the
+handles are exchanged once through ``torch.distributed`` and every peer's
+buffer is mapped into this process.  ``RowParallelLinear`` writes its partial
+GEMM output into ``partial`` and ``RMSNorm`` recognises that tensor and
+launches the fused kernel, so the sequence of modules (and needle's module
+API) is unchanged.  All pointers are fixed for the life of the object, so the
+launches can be captured in CUDA graphs.  Calls with more tokens than the
+buffers hold fall back to NCCL.
 """
 from __future__ import annotations
 
@@ -26,7 +27,6 @@ import torch.distributed as dist
 
 from .. import _lib as L
 
-_FLAG_BYTES = 2 * 1024 * 8 * 4      # [2 barriers][1024 rows per rank][8 ranks] uint32
 _MAX_ROWS_PER_RANK = 1024
 _MAX_WORLD = 8
 _MAX_HIDDEN = 8192
@@ -56,19 +56,20 @@ class TPComm:
         self.hidden, self.dtype = hidden, dtype
         self.device = torch.device(device)
         self.max_tokens = min(int(max_tokens), _MAX_ROWS_PER_RANK * self.world)
-        esz = torch.empty((), dtype=dtype).element_size()
-        n = -(-self.max_tokens * hidden * esz // 256) * 256
-        total = -(-(_FLAG_BYTES + 3 * n) // _SEGMENT) * _SEGMENT
-        self._buf = torch.zeros(total, dtype=torch.uint8, device=self.device)
-        self.epochs = torch.zeros(_MAX_ROWS_PER_RANK, dtype=torch.int32, device=self.device)
-        torch.cuda.synchronize(self.device)  # zeroed flags before any peer can see them
-
-        def view(off):
-            return self._buf[off:off + self.max_tokens * hidden * esz].view(dtype).view(
-                self.max_tokens, hidden)
-        self.partial = view(_FLAG_BYTES)
-        self.out = view(_FLAG_BYTES + n)
-        self.residual = view(_FLAG_BYTES + 2 * n)
+        # local: partial sums (the GEMM writes here), normalised output, residual
+        mk = lambda: torch.zeros(self.max_tokens, hidden, dtype=dtype, device=self.device)
+        self.partial, self.out, self.residual = mk(), mk(), mk()
+        # shared: receive slots [2][world][slot_rows][hidden], then gather
+        # slots [2][world][slot_rows][2][hidden]
+        esz = self.partial.element_size()
+        self.slot_rows = -(-self.max_tokens // self.world)
+        n_recv = 2 * self.world * self.slot_rows * hidden * esz
+        n_gather = 2 * n_recv
+        total = -(-(n_recv + n_gather) // _SEGMENT) * _SEGMENT
+        self._buf = torch.full((total,), 0xFF, dtype=torch.uint8, device=self.device)
+        # per-row-index call counters of the kernel's two CTA roles
+        self.epochs = torch.zeros(2 * _MAX_ROWS_PER_RANK, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)  # sentinels in place before any peer can write
 
         lib = L.lib()
         handle = (ctypes.c_char * 64)()
@@ -89,10 +90,8 @@ class TPComm:
             self._opened.append(ptr.value)
             bases.append(ptr.value + off)
         W = self.world
-        self._flags = (ctypes.c_void_p * W)(*[b for b in bases])
-        self._parts = (ctypes.c_void_p * W)(*[b + _FLAG_BYTES for b in bases])
-        self._outs = (ctypes.c_void_p * W)(*[b + _FLAG_BYTES + n for b in bases])
-        self._ress = (ctypes.c_void_p * W)(*[b + _FLAG_BYTES + 2 * n for b in bases])
+        self._recv = (ctypes.c_void_p * W)(*bases)
+        self._gather = (ctypes.c_void_p * W)(*[b + n_recv for b in bases])
         self._epochs = ctypes.cast(ctypes.c_void_p(self.epochs.data_ptr()),
                                    ctypes.POINTER(ctypes.c_uint))
         dist.barrier(group=group)  # every rank has mapped every buffer
@@ -118,10 +117,10 @@ class TPComm:
             raise TypeError("weight must be contiguous and of the buffers' dtype")
         stream = torch.cuda.current_stream(self.device).cuda_stream
         L.check(L.lib().nb_tp_allreduce_add_rmsnorm(
-            ctypes.cast(self._parts, ctypes.c_void_p), ctypes.cast(self._outs, ctypes.c_void_p),
-            ctypes.cast(self._ress, ctypes.c_void_p), ctypes.cast(self._flags, ctypes.c_void_p),
-            self._epochs, self.rank, self.world, weight.data_ptr(), T, self.hidden, float(eps),
-            2 if self.dtype == torch.bfloat16 else 1, stream))
+            self.partial.data_ptr(), ctypes.cast(self._recv, ctypes.c_void_p),
+            ctypes.cast(self._gather, ctypes.c_void_p), self.slot_rows, self.out.data_ptr(),
+            self.residual.data_ptr(), self._epochs, self.rank, self.world, weight.data_ptr(), T,
+            self.hidden, float(eps), 2 if self.dtype == torch.bfloat16 else 1, stream))
         return self.out[:T], res
 
     def close(self) -> None:

@@ -10,11 +10,12 @@ the expected result is computed on the CPU:
 * the normalised output follows needle's RMSNorm (``needle/layers/norm.py``);
   the fp32 sum of squares runs in another order, so it is compared within one
   bf16 ulp (tolerance 2e-2 absolute on values of order 1-4);
-* both ranks must hold identical bits (each computes its own rows and stores
-  them into every rank's buffers).
+* both ranks must hold identical bits (each owner computes its rows once and
+  pushes them to every rank).
 
-Calls of different row counts exercise the per-row epochs; a CUDA graph
-replays the launch with new data.  The model test runs a TP=2 bf16 decode
+Calls of different row counts exercise the per-row call counters and the
+double-buffered slots; a partial holding the exchange's sentinel NaN pattern
+must come out as a NaN; a CUDA graph replays the launch with new data.  The model test runs a TP=2 bf16 decode
 with the fused path and with NCCL and compares the logits.  NVLS is off for
 these multi-process runs.  Skipped with fewer than two GPUs.
 """
@@ -79,6 +80,22 @@ def _op_worker(rank, world, port, q):
             out, h = comm.allreduce_add_rmsnorm(T, res.to(dev), wd, EPS)
             check(T, call, out, h)
 
+        # a partial holding the exchange's sentinel bit pattern (a NaN) must
+        # arrive as a NaN, not stall the exchange
+        T = 5
+        parts, res, w = _inputs(T, 50, world)
+        p_local = parts[rank].clone()
+        if rank == 0:
+            p_local.view(torch.int16)[2, 17] = -1  # 0xFFFF
+        comm.partial[:T].copy_(p_local)
+        out, h = comm.allreduce_add_rmsnorm(T, res.to(dev), w.to(dev), EPS)
+        y_ref, h_ref = _expected(parts, res, w)
+        h_c, out_c = h.cpu(), out.cpu()
+        other = [0, 1, 3, 4]
+        report.append((T, 50, bool(torch.isnan(h_c[2, 17]) and torch.isnan(out_c[2]).all()
+                                   and torch.equal(h_c[other], h_ref[other])),
+                       float((out_c[other].float() - y_ref[other].float()).abs().max()), True))
+
         # CUDA graph: capture one launch (plus the copies feeding it), replay with new data
         T = 48
         src = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev)
@@ -135,7 +152,7 @@ def test_fused_allreduce_rmsnorm_matches_cpu(cuda):
     res = _run(_op_worker, 2)
     for r, (report, errs) in res.items():
         assert errs == 0, (r, errs)
-        assert len(report) == len(ROWS) + 3
+        assert len(report) == len(ROWS) + 4
         for T, call, h_exact, y_err, same in report:
             assert h_exact, (r, T, call, "residual not bit-identical")
             assert y_err <= 2e-2, (r, T, call, y_err)
