@@ -50,10 +50,12 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample budget (rank 0, N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode-op", "llama8b", "qwen72b", "prefill"],
+    ap.add_argument("--workload",
+                    choices=["decode-op", "llama8b", "qwen72b", "prefill", "allreduce"],
                     default="decode-op",
                     help="decode-op: config 2 (default); llama8b: config 3 at N=1, config 4 "
-                         "(tp=N) at N>1; qwen72b: config 5 (tp=N, N>=4)")
+                         "(tp=N) at N>1; qwen72b: config 5 (tp=N, N>=4); allreduce: the TP "
+                         "all-reduce + residual + RMSNorm per call, fused kernel vs NCCL")
     return ap.parse_args()
 
 
@@ -595,12 +597,104 @@ def run_prefill(args):
         dist.destroy_process_group()
 
 
+def run_allreduce(args):
+    """Per-call latency of the TP all-reduce + residual add + RMSNorm at the
+    decode shapes of configs 5 (128 rows x 8192) and 4 (512 x 4096), and a
+    16-row case: the fused NVLink kernel against NCCL all-reduce + the
+    fused add+RMSNorm kernel.  Each is timed as CUDA-graph replays of 50
+    back-to-back calls (device events, max over ranks)."""
+    rank, local, ws = dist_init(args.gpus)
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    import torch.distributed as dist
+    if ws == 1:  # a one-rank group: the kernel exchanges with itself
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29599")
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+    from needle_b200 import ops
+    from needle_b200.layers.tp_comm import TPComm
+    calls, reps, W = 50, max(1, args.steps // 50), max(3, args.warmup)
+    shapes = [("config5", 128, 8192), ("config4", 512, 4096), ("small", 16, 8192)]
+    res = {}
+    launches = 0
+    for name, T, H in shapes:
+        comm = TPComm(T, H, torch.bfloat16, dev)
+        g = torch.Generator(device=dev).manual_seed(rank)
+        comm.partial.normal_(generator=g)
+        comm.residual.normal_(generator=g)
+        w = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        x = torch.randn(T, H, dtype=torch.bfloat16, device=dev, generator=g)
+        r = torch.randn_like(x)
+        o = torch.empty_like(x)
+
+        def fused():
+            for _ in range(calls):
+                comm.allreduce_add_rmsnorm(T, comm.residual[:T], w, 1e-6)
+
+        def nccl():
+            for _ in range(calls):
+                dist.all_reduce(x)
+                ops.fused_add_rmsnorm(x, r, w, 1e-6, out=o, residual_out=r)
+        for label, fn in (("fused", fused), ("nccl", nccl)):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            for _ in range(W):
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            barrier(ws)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            us = max_over_ranks(e0.elapsed_time(e1) / (reps * calls) * 1e3, ws, dev)
+            res[f"{name}_{label}_us"] = round(us, 2)
+            if label == "fused":
+                launches += reps * calls
+            del graph
+        # algorithmic NVLink bytes per rank per call: reduce-scatter push of
+        # (W-1)/W of the partial, all-gather push of the residual and normalised rows
+        nvl = 3 * (ws - 1) / ws * T * H * 2
+        res[f"{name}_nvlink_bytes_per_rank"] = int(nvl)
+        barrier(ws)
+        comm.close()
+    errs = ops.device_errors()
+    if rank == 0:
+        t = res["config5_fused_us"]
+        gbs = res["config5_nvlink_bytes_per_rank"] / (t * 1e-6) / 1e9
+        print(json.dumps({
+            "metric": "TP all-reduce + residual + RMSNorm, us per call (config 5 decode shape)",
+            "value": t, "unit": "us", "n_gpus": ws, "steps": reps * calls, "warmup": W,
+            "ms_per_step": round(t / 1e3, 5), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,1))",
+            "config": {"workload": "allreduce: 128 x 8192 (config 5), 512 x 4096 (config 4), "
+                                   "16 x 8192 rows per call; CUDA graphs of 50 calls",
+                       "parallelism": f"tp{ws}"},
+            "roofline": {"bound": "nvlink", "achieved": round(gbs, 1), "peak": 770.0,
+                         "unit": "GB/s", "frac": round(gbs / 770.0, 4),
+                         "peak_source": "measured peer copy per direction (pool figure)",
+                         "traffic": None},
+            "shapes": res, "device_errors": errs, "gpu_launches": launches}), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "allreduce":
+        run_allreduce(args)
     elif args.workload != "decode-op":
         run_model(args)
     else:
