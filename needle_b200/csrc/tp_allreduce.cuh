@@ -75,36 +75,37 @@ __device__ __forceinline__ uint4 canon(uint4 v) {
   return make_uint4(canon_word(v.x), canon_word(v.y), canon_word(v.z), canon_word(v.w));
 }
 
-// Re-poll a 16-byte vector that had not arrived at the first look, until it
-// arrives; gives up (dead = true) after kWaitLimitNs, or at once if an
-// earlier wait of this thread already gave up.
-__device__ __forceinline__ uint4 wait_vec_slow(const void* p, bool* dead) {
-  uint4 v = make_uint4(0, 0, 0, 0);
-  if (*dead) return v;
-  const unsigned long long t0 = globaltimer();
-  for (;;) {
-    v = ld_volatile_v4(p);
-    if (arrived(v)) return v;
-    if (globaltimer() - t0 > kWaitLimitNs) {
-      *dead = true;
-      return v;
-    }
-  }
-}
-
 // N vectors at base + i * stride (elements of 16-bit T), i < n: all loads in
-// flight at once (one memory round trip when everything has arrived), then
-// the stragglers one by one.  Each slot is reset to the sentinel after it is
-// read.
+// flight at once; while some have not arrived, all of the missing ones are
+// loaded again together, so every pass costs one memory round trip however
+// many senders are late.  Gives up (dead = true) after kWaitLimitNs, or at
+// once if an earlier wait of this thread already gave up.  Each slot is reset
+// to the sentinel after it is read.
 template <int N, typename T>
 __device__ __forceinline__ void gather_vecs(T* base, int64_t stride, int n, uint4 (&v)[N],
                                             bool& dead) {
+  unsigned missing = 0;
 #pragma unroll
   for (int i = 0; i < N; ++i)
     if (i < n) v[i] = ld_volatile_v4(base + i * stride);
 #pragma unroll
   for (int i = 0; i < N; ++i)
-    if (i < n && !arrived(v[i])) v[i] = wait_vec_slow(base + i * stride, &dead);
+    if (i < n && !arrived(v[i])) missing |= 1u << i;
+  if (missing && !dead) {
+    const unsigned long long t0 = globaltimer();
+    while (missing) {
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if (missing & (1u << i)) v[i] = ld_volatile_v4(base + i * stride);
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if ((missing & (1u << i)) && arrived(v[i])) missing &= ~(1u << i);
+      if (missing && globaltimer() - t0 > kWaitLimitNs) {
+        dead = true;
+        break;
+      }
+    }
+  }
   const uint4 sentinel = make_uint4(kArSentinel, kArSentinel, kArSentinel, kArSentinel);
 #pragma unroll
   for (int i = 0; i < N; ++i)
@@ -137,8 +138,6 @@ __global__ void __launch_bounds__(1024)
   unsigned* ep = epochs + role * kArMaxRows;  // per-role call counters
   bool dead = false;
   uint4 v[kArMaxRanks];
-  uint4 w4 = make_uint4(0, 0, 0, 0);
-  if (role == 0 && mine) w4 = __ldg(reinterpret_cast<const uint4*>(weight + col));
   // The grid is at most what fits on the GPU at once (every CTA resident), so
   // a CTA waiting on a peer never blocks the CTA that the peer waits for.
   for (int b = blockIdx.x - role * G; b < per; b += G) {
@@ -175,10 +174,10 @@ __global__ void __launch_bounds__(1024)
           T rv[VEC];
           *reinterpret_cast<uint4*>(rv) =
               *reinterpret_cast<const uint4*>(res + (int64_t)row * hidden + col);
+          gather_vecs<kArMaxRanks>(rb, slot, world, v, dead);  // slots reset for two calls later
           float acc[VEC];
 #pragma unroll
           for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
-          gather_vecs<kArMaxRanks>(rb, slot, world, v, dead);  // slots reset for two calls later
 #pragma unroll
           for (int p = 0; p < kArMaxRanks; ++p) {  // fixed rank order: identical bits everywhere
             if (p < world) {
@@ -196,6 +195,9 @@ __global__ void __launch_bounds__(1024)
             ss = __fadd_rn(ss, __fmul_rn(f, f));
           }
         }
+        // the weight load's latency hides behind the block reduction
+        uint4 w4 = make_uint4(0, 0, 0, 0);
+        if (mine) w4 = __ldg(reinterpret_cast<const uint4*>(weight + col));
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
