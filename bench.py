@@ -51,11 +51,13 @@ def parse():
                     help="CPU-baseline sample budget (rank 0, N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload",
-                    choices=["decode-op", "llama8b", "qwen72b", "prefill", "allreduce"],
+                    choices=["decode-op", "llama8b", "qwen72b", "prefill", "allreduce",
+                             "store-kv"],
                     default="decode-op",
                     help="decode-op: config 2 (default); llama8b: config 3 at N=1, config 4 "
                          "(tp=N) at N>1; qwen72b: config 5 (tp=N, N>=4); allreduce: the TP "
-                         "all-reduce + residual + RMSNorm per call, fused kernel vs NCCL")
+                         "all-reduce + residual + RMSNorm per call, fused kernel vs NCCL; store-kv: "
+                         "the prefill-size paged KV write (T=8192)")
     return ap.parse_args()
 
 
@@ -512,17 +514,91 @@ def run_model(args):
             "e2e": {"value": round(value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": B * (8 + 8 + 4 + 4) + B * 4 * (len(seqs[0].token_ids) // 16 + 1),
                     "d2h_bytes_per_step": B * 8},
-            "cpu_baseline": None,
+            "cpu_baseline": None,  # filled in below, after the process group is gone
             # our kernels per decode step: first RMSNorm, per layer RoPE+KV-write,
             # paged decode (+ merge when split), 2 fused add+RMSNorm, SwiGLU
             "gpu_launches": K * (cfg.num_hidden_layers * (5 + (1 if _splits(runner, seqs) > 1 else 0)) + 1),
             "clocks": clocks.summary(),
         }
-        print(json.dumps(line), flush=True)
+    ctx_now = [len(s.token_ids) - 1 for s in seqs]
     runner.close()
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            del runner, drv
+            torch.cuda.empty_cache()
+            line["cpu_baseline"] = cpu_baseline_model(cfg, ctx_now, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_model(cfg, ctx_lens, budget_s):
+    """needle's decode step on the host cores, EXTRAPOLATED: one decoder layer
+    of the full (unsharded) model at the real batch and context lengths,
+    through needle's CPU path as restated in oracle/ (RMSNorm, the q/k/v/o and
+    MLP GEMMs, RoPE, the decode KV write and ``_decode_pytorch``), timed and
+    multiplied by the layer count; plus the lm_head GEMM over 1/8 of the
+    vocabulary, multiplied by 8.  Weights and cache hold zeros: the CPU
+    kernels' time does not depend on the values."""
+    import torch.nn.functional as F
+    from oracle import needle_oracle as no
+    torch.set_num_threads(os.cpu_count() or 1)
+    dt = torch.bfloat16
+    B = len(ctx_lens)
+    H, kv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    hid, inter, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
+    nb = [(c + 1 + 15) // 16 for c in ctx_lens]   # blocks after the new token's write
+    N = sum(nb) + 1
+    cache = torch.zeros(2, N, kv, 16, D, dtype=dt)
+    bt = torch.full((B, max(nb)), N - 1, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(nb):
+        bt[i, :n] = torch.arange(o, o + n, dtype=torch.int32)
+        o += n
+    ctx = torch.tensor(ctx_lens, dtype=torch.int32)
+    z = lambda *shape: torch.zeros(*shape, dtype=dt)
+    bias = cfg.model_type == "qwen2"
+    qw, kw, vw, ow = z(H * D, hid), z(kv * D, hid), z(kv * D, hid), z(hid, H * D)
+    qb, kb, vb = (z(H * D), z(kv * D), z(kv * D)) if bias else (None, None, None)
+    gw, uw, dw = z(inter, hid), z(inter, hid), z(hid, inter)
+    nw = torch.ones(hid, dtype=dt)
+    cos_t, sin_t = no.rope_cache(D, max(ctx_lens) + 2, cfg.rope_theta)
+    cos, sin = cos_t[ctx.long()].to(dt), sin_t[ctx.long()].to(dt)
+    h = torch.randn(B, hid).to(dt)
+    scale = no.default_scale(D)
+
+    def layer():
+        x = no.rms_norm(h, nw, eps)
+        q = F.linear(x, qw, qb).view(B, H, D)
+        k = F.linear(x, kw, kb).view(B, kv, D)
+        v = F.linear(x, vw, vb).view(B, kv, D)
+        q, k = no.apply_rope(q, k, cos, sin)
+        no.decode_write_kv(k, v, cache, bt, ctx)
+        a = no.decode_attention(q, cache, bt, ctx, scale, H, kv, D)
+        h2 = h + F.linear(a.reshape(B, H * D), ow)
+        x = no.rms_norm(h2, nw, eps)
+        return h2 + F.linear(F.silu(F.linear(x, gw)) * F.linear(x, uw), dw)
+
+    times = []
+    t_all = time.time()
+    while not times or (time.time() - t_all < budget_s and len(times) < 5):
+        t0 = time.time()
+        layer()
+        times.append(time.time() - t0)
+    t_layer = statistics.median(times)
+    slice_v = -(-cfg.vocab_size // 8)
+    hw = z(slice_v, hid)
+    t0 = time.time()
+    F.linear(h, hw)
+    t_head = (time.time() - t0) * 8
+    step = cfg.num_hidden_layers * t_layer + t_head
+    return {"value": round(B / step, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "extrapolated": True,
+            "sample": f"one decoder layer of the full model at B={B}, mean ctx "
+                      f"{sum(ctx_lens) / B:.0f}: {len(times)} runs, median {t_layer:.2f} s, "
+                      f"x{cfg.num_hidden_layers} layers; lm_head over 1/8 of the vocabulary "
+                      f"{t_head / 8:.2f} s x8; step {step:.1f} s"}
 
 
 def _splits(runner, seqs) -> int:
@@ -687,6 +763,85 @@ def run_allreduce(args):
     dist.destroy_process_group()
 
 
+def run_store_kv(args):
+    """The prefill-size paged KV write: 8 sequences x 1024 new tokens
+    (T = 8192), 8 KV heads, D = 128, bf16, into a 20000-block pool with
+    shuffled block tables (`_write_kv`, needle/layers/attention.py:204-246).
+    Algorithmic bytes = 2·T·kv·D·2 read + the same written = 64 MiB.  The
+    launches rotate over 4 input sets (separate k/v/q tensors and disjoint
+    block sets: 256 MiB of K/V traffic, 2x the L2) and are timed back to back
+    with one event pair, so no launch finds its data in L2.  The fused RoPE +
+    KV write of the same step (q in place, k rotated, K/V stored) is timed
+    the same way."""
+    rank, local, ws = dist_init(args.gpus)
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    from needle_b200 import ops
+    B, S, H, KV, D, N, bs, NS = 8, 1024, 32, 8, 128, 20000, 16, 4
+    T = B * S
+    g = torch.Generator(device=dev).manual_seed(0)
+    mk = lambda h: torch.randn(T, h, D, device=dev, generator=g, dtype=torch.bfloat16)
+    ks, vs, qs = [mk(KV) for _ in range(NS)], [mk(KV) for _ in range(NS)], [mk(H) for _ in range(NS)]
+    cache = torch.zeros(2, N, KV, bs, D, device=dev, dtype=torch.bfloat16)
+    maxb = S // bs
+    perm = torch.randperm(N, generator=torch.Generator().manual_seed(0))[:NS * B * maxb]
+    bts = [perm[i * B * maxb:(i + 1) * B * maxb].view(B, maxb).to(device=dev, dtype=torch.int32)
+           for i in range(NS)]
+    ctx = torch.zeros(B, dtype=torch.int32, device=dev)
+    cu = torch.arange(0, T + 1, S, dtype=torch.int32, device=dev)
+    pos = torch.arange(S, device=dev).repeat(B)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32, device=dev) / D))
+    fr = pos[:, None].float() * inv[None, :]
+    emb = torch.cat([fr, fr], dim=-1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    st = torch.cuda.current_stream(dev)
+    W, K = max(3, args.warmup), max(NS, min(args.steps, 200))
+
+    def timed(fn):
+        for i in range(W * NS):
+            fn(i % NS)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(st)
+        for i in range(K):
+            fn(i % NS)
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / K
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    with clocks:
+        barrier(ws)
+        t_store = timed(lambda i: ops.store_kvcache(ks[i], vs[i], cache, bts[i], ctx, cu))
+        t_rope = timed(lambda i: ops.rope_store_kvcache(qs[i], ks[i], vs[i], cos, sin, cache,
+                                                        bts[i], ctx, cu))
+        barrier(ws)
+    t_store = max_over_ranks(t_store, ws, dev)
+    t_rope = max_over_ranks(t_rope, ws, dev)
+    peak, src = measured_hbm_peak()
+    store_bytes = 2 * (2 * T * KV * D * 2)
+    rope_bytes = 2 * T * H * D * 2 + 2 * T * KV * D * 2 + 2 * T * KV * D * 2 + 2 * T * D * 2
+    gbs = store_bytes / (t_store * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "paged KV write GB/s (prefill-size, T=8192)", "value": round(gbs, 1),
+            "unit": "GB/s", "n_gpus": ws, "steps": K, "warmup": W * NS,
+            "ms_per_step": round(t_store, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,1))",
+            "config": {"workload": "store-kv: 8 x 1024 new tokens, kv=8, D=128, 20000-block pool, "
+                                   "shuffled block tables; 4 rotating input sets (256 MiB of "
+                                   "K/V traffic > L2), launches back to back"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_source": src,
+                         "bytes_per_launch": store_bytes, "traffic": None},
+            "rope_store": {"ms": round(t_rope, 5), "bytes_per_launch": rope_bytes,
+                           "GB/s": round(rope_bytes / (t_rope * 1e-3) / 1e9, 1),
+                           "frac": round(rope_bytes / (t_rope * 1e-3) / 1e9 / peak, 4)},
+            "gpu_launches": 2 * K, "clocks": clocks.summary()}), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -695,6 +850,8 @@ def main():
         run_prefill(args)
     elif args.workload == "allreduce":
         run_allreduce(args)
+    elif args.workload == "store-kv":
+        run_store_kv(args)
     elif args.workload != "decode-op":
         run_model(args)
     else:

@@ -1,9 +1,13 @@
 // store_kvcache, RoPE, and RoPE fused with the KV store.
 //
-// All three are HBM-bound elementwise/scatter kernels: one 16-byte vector per
-// thread, consecutive threads on consecutive vectors of one head row so that
-// both the token-major reads and the cache-row writes are coalesced.
+// All three are HBM-bound elementwise/scatter kernels on 16-byte vectors,
+// consecutive threads on consecutive vectors of one head row so that both the
+// token-major reads and the cache-row writes are coalesced.  The cache writers
+// give each CTA a few tokens and resolve each token's slot once, in shared
+// memory, before the copy.
 #pragma once
+#include <algorithm>
+
 #include "nb_common.cuh"
 
 namespace nb {
@@ -48,33 +52,91 @@ __device__ __forceinline__ bool token_slot(int t, const int32_t* __restrict__ cu
   return true;
 }
 
+constexpr int kMaxTokPerCta = 64;
+
+// Slots of this CTA's tokens [t0, t0 + nt) into shared memory, one thread per
+// token (phys = -1: the token is not written).  Computing them once per token
+// instead of once per 16-byte vector keeps the dependent index loads
+// (cu_seqlens search, context_lens, block table) off the copy threads.
+__device__ __forceinline__ void cta_token_slots(int t0, int nt, const int32_t* __restrict__ cu,
+                                                const int32_t* __restrict__ ctx, int num_seqs,
+                                                const int32_t* __restrict__ bt,
+                                                int64_t bt_stride, int maxb, int num_blocks,
+                                                int block_size, int* s_phys, int* s_off) {
+  if (threadIdx.x < nt) {
+    int phys = -1, off = 0;
+    if (!token_slot(t0 + threadIdx.x, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks,
+                    block_size, phys, off))
+      phys = -1;
+    s_phys[threadIdx.x] = phys;
+    s_off[threadIdx.x] = off;
+  }
+  __syncthreads();
+}
+
+// K/V rows of tok_per_cta tokens per CTA.  Items are 16-byte vectors ordered
+// (token, head, K/V, vector) so consecutive threads read consecutive vectors
+// of a token row and write consecutive vectors of a cache row.  The sources
+// do not depend on the slots: every thread issues its first U loads, then the
+// CTA resolves its tokens' slots while those loads are in flight, then stores.
 template <typename T>
 __global__ void __launch_bounds__(256)
     store_kvcache_kernel(const T* __restrict__ k, int64_t k_stride, const T* __restrict__ v,
                          int64_t v_stride, T* __restrict__ cache, int num_blocks, int kvh,
                          int block_size, int D, const int32_t* __restrict__ bt, int64_t bt_stride,
                          int maxb, const int32_t* __restrict__ cu, const int32_t* __restrict__ ctx,
-                         int num_seqs, int num_tokens) {
+                         int num_seqs, int num_tokens, int tok_per_cta) {
   griddep_launch_dependents();  // the paged decode that follows may start its launch
+  __shared__ int s_phys[kMaxTokPerCta], s_off[kMaxTokPerCta];
   constexpr int VEC = 16 / sizeof(T);
-  const int vpr = D / VEC;                       // vectors per head row
-  const int64_t total = (int64_t)num_tokens * kvh * 2 * vpr;
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (gid >= total) return;
-  const int vec = (int)(gid % vpr);
-  int64_t r = gid / vpr;
-  const int which = (int)(r & 1);               // 0 = K, 1 = V
-  r >>= 1;
-  const int h = (int)(r % kvh);
-  const int t = (int)(r / kvh);
-  int phys, off;
-  if (!token_slot(t, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, phys, off))
-    return;
-  const T* src = which ? v + (int64_t)t * v_stride : k + (int64_t)t * k_stride;
-  src += (int64_t)h * D + vec * VEC;
-  T* dst = cache + ((((int64_t)which * num_blocks + phys) * kvh + h) * block_size + off) * D +
-           vec * VEC;
-  *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(src));
+  constexpr int U = 4;
+  const int vpr = D / VEC;  // vectors per head row
+  const int t0 = blockIdx.x * tok_per_cta;
+  const int nt = min(tok_per_cta, num_tokens - t0);
+  const int items = nt * kvh * 2 * vpr;
+  uint4 val[U];
+  auto load = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * blockDim.x;
+      if (idx < items) {
+        const int vec = idx % vpr;
+        int r = idx / vpr;
+        const int which = r & 1;  // 0 = K, 1 = V
+        r >>= 1;
+        const int64_t t = t0 + r / kvh;
+        const T* src = (which ? v + t * v_stride : k + t * k_stride) + (int64_t)(r % kvh) * D +
+                       vec * VEC;
+        val[u] = __ldg(reinterpret_cast<const uint4*>(src));
+      }
+    }
+  };
+  auto store = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * blockDim.x;
+      if (idx < items) {
+        const int vec = idx % vpr;
+        int r = idx / vpr;
+        const int which = r & 1;
+        r >>= 1;
+        const int h = r % kvh, lt = r / kvh;
+        const int phys = s_phys[lt];
+        if (phys >= 0)
+          *reinterpret_cast<uint4*>(
+              cache + ((((int64_t)which * num_blocks + phys) * kvh + h) * block_size + s_off[lt]) * D +
+              vec * VEC) = val[u];
+      }
+    }
+  };
+  load(threadIdx.x);
+  cta_token_slots(t0, nt, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, s_phys,
+                  s_off);
+  store(threadIdx.x);
+  for (int base = threadIdx.x + U * blockDim.x; base < items; base += U * blockDim.x) {
+    load(base);
+    store(base);
+  }
 }
 
 // Scalar fallback for shapes whose rows are not 16-byte vectorisable.
@@ -179,9 +241,32 @@ __global__ void __launch_bounds__(256)
                        c * VEC);
 }
 
-// RoPE of q (in place) and k, then K/V into the cache.  Rows are processed as
-// (token, head slot) with head slots [0, Hq) = q, [Hq, Hq+Hkv) = k and
-// [Hq+Hkv, Hq+2Hkv) = v.
+// Load / store VEC consecutive elements (one 16-byte vector when VEC fills one).
+template <typename T, int VEC>
+__device__ __forceinline__ void ld_chunk(T (&x)[VEC], const T* p) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    *reinterpret_cast<uint4*>(x) = *reinterpret_cast<const uint4*>(p);
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) x[e] = p[e];
+  }
+}
+template <typename T, int VEC>
+__device__ __forceinline__ void st_chunk(T* p, const T (&x)[VEC]) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(x);
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) p[e] = x[e];
+  }
+}
+
+// RoPE of q (in place) and k, then K/V into the cache, tok_per_cta tokens per
+// CTA.  Items are (token, head slot, chunk) with head slots [0, Hq) = q,
+// [Hq, Hq+Hkv) = k and [Hq+Hkv, Hq+2Hkv) = v; a chunk is VEC element pairs
+// (x[j..j+VEC), x[j+D/2..j+D/2+VEC)).  q chunks are rotated and written back
+// at once; k/v chunks are loaded (k rotated) before the CTA resolves its
+// tokens' slots, and stored to the cache after.
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256)
     rope_store_kernel(T* q, int64_t q_stride, int hq, T* k, int64_t k_stride,
@@ -190,56 +275,90 @@ __global__ void __launch_bounds__(256)
                       int num_blocks, int hk, int block_size, int D,
                       const int32_t* __restrict__ bt, int64_t bt_stride, int maxb,
                       const int32_t* __restrict__ cu, const int32_t* __restrict__ ctx,
-                      int num_seqs, int num_tokens, int write_k_back) {
+                      int num_seqs, int num_tokens, int write_k_back, int tok_per_cta) {
   griddep_launch_dependents();  // the paged decode that follows may start its launch
+  __shared__ int s_phys[kMaxTokPerCta], s_off[kMaxTokPerCta];
+  constexpr int U = 1;  // one chunk per thread: more threads in flight beat deeper ones here
   const int half = D / 2;
   const int cpr = half / VEC;
   const int heads = hq + 2 * hk;
-  const int64_t total = (int64_t)num_tokens * heads * cpr;
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (gid >= total) return;
-  const int c = (int)(gid % cpr);
-  const int64_t r = gid / cpr;
-  const int hh = (int)(r % heads);
-  const int t = (int)(r / heads);
-  const int j = c * VEC;
-  if (hh < hq) {
-    rope_row_vec<T, VEC>(q + (int64_t)t * q_stride + (int64_t)hh * D,
-                         cos + (int64_t)t * cs_stride, sin + (int64_t)t * cs_stride, half, j);
-    return;
-  }
-  int phys, off;
-  const bool ok =
-      token_slot(t, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, phys, off);
-  const bool is_k = hh < hq + hk;
-  const int h = is_k ? hh - hq : hh - hq - hk;
-  T lo[VEC], hi[VEC];
-  if (is_k) {
-    T* row = k + (int64_t)t * k_stride + (int64_t)h * D;
-    const T* cs = cos + (int64_t)t * cs_stride;
-    const T* sn = sin + (int64_t)t * cs_stride;
+  const int t0 = blockIdx.x * tok_per_cta;
+  const int nt = min(tok_per_cta, num_tokens - t0);
+  const int items = nt * heads * cpr;
+  T lo[U][VEC], hi[U][VEC];
+  auto load = [&](int base) {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      float ol, oh;
-      rope_pair<T>(Dt<T>::to_f(row[j + e]), Dt<T>::to_f(row[j + half + e]),
-                   Dt<T>::to_f(cs[j + e]), Dt<T>::to_f(cs[j + half + e]),
-                   Dt<T>::to_f(sn[j + e]), Dt<T>::to_f(sn[j + half + e]), ol, oh);
-      lo[e] = Dt<T>::from_f(ol);
-      hi[e] = Dt<T>::from_f(oh);
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * blockDim.x;
+      if (idx >= items) continue;
+      const int c = idx % cpr;
+      const int r = idx / cpr;
+      const int hh = r % heads;
+      const int64_t t = t0 + r / heads;
+      const int j = c * VEC;
+      if (hh < hq) {
+        rope_row_vec<T, VEC>(q + t * q_stride + (int64_t)hh * D, cos + t * cs_stride,
+                             sin + t * cs_stride, half, j);
+      } else if (hh < hq + hk) {
+        T* row = k + t * k_stride + (int64_t)(hh - hq) * D;
+        const T* cs = cos + t * cs_stride;
+        const T* sn = sin + t * cs_stride;
+        T cl[VEC], ch[VEC], sl[VEC], sh[VEC];
+        ld_chunk<T, VEC>(lo[u], row + j);
+        ld_chunk<T, VEC>(hi[u], row + j + half);
+        ld_chunk<T, VEC>(cl, cs + j);
+        ld_chunk<T, VEC>(ch, cs + j + half);
+        ld_chunk<T, VEC>(sl, sn + j);
+        ld_chunk<T, VEC>(sh, sn + j + half);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          float ol, oh;
+          rope_pair<T>(Dt<T>::to_f(lo[u][e]), Dt<T>::to_f(hi[u][e]), Dt<T>::to_f(cl[e]),
+                       Dt<T>::to_f(ch[e]), Dt<T>::to_f(sl[e]), Dt<T>::to_f(sh[e]), ol, oh);
+          lo[u][e] = Dt<T>::from_f(ol);
+          hi[u][e] = Dt<T>::from_f(oh);
+        }
+        if (write_k_back) {
+          st_chunk<T, VEC>(row + j, lo[u]);
+          st_chunk<T, VEC>(row + j + half, hi[u]);
+        }
+      } else {
+        const T* row = v + t * v_stride + (int64_t)(hh - hq - hk) * D;
+        ld_chunk<T, VEC>(lo[u], row + j);
+        ld_chunk<T, VEC>(hi[u], row + j + half);
+      }
     }
-    if (write_k_back) {
+  };
+  auto store = [&](int base) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) { row[j + e] = lo[e]; row[j + half + e] = hi[e]; }
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * blockDim.x;
+      if (idx >= items) continue;
+      const int c = idx % cpr;
+      const int r = idx / cpr;
+      const int hh = r % heads;
+      const int lt = r / heads;
+      if (hh < hq) continue;
+      const bool is_k = hh < hq + hk;
+      const int h = is_k ? hh - hq : hh - hq - hk;
+      const int phys = s_phys[lt];
+      if (phys < 0) continue;
+      T* dst = cache +
+               ((((int64_t)(is_k ? 0 : 1) * num_blocks + phys) * hk + h) * block_size + s_off[lt]) *
+                   D +
+               c * VEC;
+      st_chunk<T, VEC>(dst, lo[u]);
+      st_chunk<T, VEC>(dst + half, hi[u]);
     }
-  } else {
-    const T* row = v + (int64_t)t * v_stride + (int64_t)h * D;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) { lo[e] = row[j + e]; hi[e] = row[j + half + e]; }
+  };
+  load(threadIdx.x);
+  cta_token_slots(t0, nt, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, s_phys,
+                  s_off);
+  store(threadIdx.x);
+  for (int base = threadIdx.x + U * blockDim.x; base < items; base += U * blockDim.x) {
+    load(base);
+    store(base);
   }
-  if (!ok) return;
-  T* dst = cache + ((((int64_t)(is_k ? 0 : 1) * num_blocks + phys) * hk + h) * block_size + off) * D;
-#pragma unroll
-  for (int e = 0; e < VEC; ++e) { dst[j + e] = lo[e]; dst[j + half + e] = hi[e]; }
 }
 
 }  // namespace nb
@@ -270,11 +389,13 @@ int launch_store(const void* k, int64_t ks, const void* v, int64_t vs, void* cac
                       ((uintptr_t)cache % 16 == 0);
   const int threads = 256;
   if (vec_ok) {
-    const int64_t total = (int64_t)ntok * kvh * 2 * (D / VEC);
-    const int64_t blocks = (total + threads - 1) / threads;
+    // about 1024 vectors (4 per thread) per CTA
+    const int per_tok = kvh * 2 * (D / VEC);
+    const int tok = std::max(1, std::min(nb::kMaxTokPerCta, 1024 / std::max(1, per_tok)));
+    const int64_t blocks = ((int64_t)ntok + tok - 1) / tok;
     nb::store_kvcache_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(
         (const T*)k, ks, (const T*)v, vs, (T*)cache, nblk, kvh, bs, D, bt, bts, maxb, cu, ctx,
-        nseq, ntok);
+        nseq, ntok, tok);
   } else {
     const int64_t total = (int64_t)ntok * kvh * 2 * D;
     const int64_t blocks = (total + threads - 1) / threads;
@@ -313,17 +434,28 @@ int launch_rope_store(void* q, int64_t qs, int hq, void* k, int64_t ks, const vo
                       int hk, int bs, int D, const int32_t* bt, int64_t bts, int maxb,
                       const int32_t* cu, const int32_t* ctx, int nseq, int ntok, int wkb,
                       cudaStream_t st) {
-  // The row-wise rotation of q uses 16-byte vectors when every row is aligned;
-  // the K/V rows go element-wise within a thread's chunk (still coalesced
-  // across the threads of a row).
-  constexpr int VEC = 8 / sizeof(T) > 0 ? 8 / sizeof(T) : 1;  // 2 fp32 / 4 bf16 per thread
-  if ((D / 2) % VEC != 0) return fail(NB_ERR_UNSUPPORTED, "head_dim %d not supported", D);
-  const int64_t total = (int64_t)ntok * (hq + 2 * hk) * (D / 2 / VEC);
+  if (D % 2) return fail(NB_ERR_UNSUPPORTED, "head_dim %d is odd", D);
+  // 16-byte chunks when every row and table is 16-byte aligned, else scalar.
+  constexpr int V16 = 16 / sizeof(T);
+  const bool vec_ok = ((D / 2) % V16 == 0) && (qs % V16 == 0) && (ks % V16 == 0) &&
+                      (vs % V16 == 0) && (css % V16 == 0) && ((uintptr_t)q % 16 == 0) &&
+                      ((uintptr_t)k % 16 == 0) && ((uintptr_t)v % 16 == 0) &&
+                      ((uintptr_t)cos % 16 == 0) && ((uintptr_t)sin % 16 == 0) &&
+                      ((uintptr_t)cache % 16 == 0);
   const int threads = 256;
-  nb::rope_store_kernel<T, VEC><<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
-      (T*)q, qs, hq, (T*)k, ks, (const T*)v, vs, (const T*)cos, (const T*)sin, css, (T*)cache,
-      nblk, hk, bs, D, bt, bts, maxb, cu, ctx, nseq, ntok, wkb);
-  return check_launch("rope_store_kvcache");
+  auto launch = [&](auto kern, int vec) {
+    // about 256 chunks (one per thread) per CTA
+    const int per_tok = (hq + 2 * hk) * (D / 2 / vec);
+    const int tok = std::max(1, std::min(nb::kMaxTokPerCta, 256 / std::max(1, per_tok)));
+    const int64_t blocks = ((int64_t)ntok + tok - 1) / tok;
+    kern<<<(unsigned)blocks, threads, 0, st>>>((T*)q, qs, hq, (T*)k, ks, (const T*)v, vs,
+                                               (const T*)cos, (const T*)sin, css, (T*)cache, nblk,
+                                               hk, bs, D, bt, bts, maxb, cu, ctx, nseq, ntok, wkb,
+                                               tok);
+    return check_launch("rope_store_kvcache");
+  };
+  if (vec_ok) return launch(nb::rope_store_kernel<T, V16>, V16);
+  return launch(nb::rope_store_kernel<T, 1>, 1);
 }
 
 }  // namespace nbh

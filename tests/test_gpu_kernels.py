@@ -138,12 +138,13 @@ def test_rope_bit_exact_vs_needle(cuda, dt, H, kv, D, base):
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
-def test_rope_store_fused_matches_separate(cuda, dt):
+@pytest.mark.parametrize("D", [128, 20])  # 20: rows not 16-byte vectorisable (scalar path)
+def test_rope_store_fused_matches_separate(cuda, dt, D):
     ops = _ops()
     g = torch.Generator().manual_seed(13)
     lens = [5, 33, 1, 16]
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32)
-    T, hq, kv, D, N = int(cu[-1]), 8, 2, 128, 40
+    T, hq, kv, N = int(cu[-1]), 8, 2, 40
     ctx = torch.tensor([0, 7, 100, 15], dtype=torch.int32)
     bt = torch.randperm(N, generator=g)[:4 * 9].view(4, 9).to(torch.int32)
     q = torch.randn(T, hq, D, generator=g).to(dt)
