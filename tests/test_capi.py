@@ -92,3 +92,17 @@ def test_norm_arg_checks(fn):
     rc, msg = _err(lib.nb_rmsnorm(16, 100, 16, 16, 128, 4, 128, 1e-6, L.NB_DTYPE_BF16, None))
     assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
     assert lib.nb_rmsnorm(16, 128, 16, 16, 128, 0, 128, 1e-6, L.NB_DTYPE_BF16, None) == 0
+
+
+def test_bench_cpu_baseline_model_runs_on_a_tiny_config():
+    """The extrapolated CPU leg of the model benchmarks (needle's CPU path for
+    one decoder layer, x layers, + lm_head) runs and reports its sample."""
+    import bench
+    from needle_b200.model.config import ModelConfig
+    cfg = ModelConfig(model_type="qwen2", hidden_size=64, num_hidden_layers=3,
+                      num_attention_heads=4, num_key_value_heads=2, intermediate_size=96,
+                      vocab_size=100, max_position_embeddings=512, rms_norm_eps=1e-6,
+                      rope_theta=1e6)
+    r = bench.cpu_baseline_model(cfg, [5, 40, 17], 0.5)
+    assert r["extrapolated"] is True and r["kind"] == "port" and r["value"] > 0
+    assert "x3 layers" in r["sample"]
