@@ -12,27 +12,15 @@
 
 namespace nb {
 
-// Slot of new token `t` (global token index) for cache writes.  Restates the
-// index math of needle/layers/attention.py:214-240: position = ctx + i,
-// column = position / block_size clamped to the last table column.  Returns
-// false (and records why) when the token must not be written.
-__device__ __forceinline__ bool token_slot(int t, const int32_t* __restrict__ cu,
-                                           const int32_t* __restrict__ ctx, int num_seqs,
-                                           const int32_t* __restrict__ bt, int64_t bt_stride,
-                                           int maxb, int num_blocks, int block_size, int& phys,
-                                           int& off) {
-  int s, i, len;
-  if (cu) {
-    s = seq_of_token(cu, num_seqs, t);
-    const int c0 = __ldg(cu + s);
-    i = t - c0;
-    len = __ldg(cu + s + 1) - c0;
-  } else {
-    s = t;
-    i = 0;
-    len = 1;
-  }
-  const int c = __ldg(ctx + s);
+// Slot of token i (of len new tokens) of a sequence whose context (tokens
+// already cached) is c.  Restates the index math of
+// needle/layers/attention.py:214-240: position = c + i, column = position /
+// block_size clamped to the last table column.  Returns false (and records
+// why) when the token must not be written.
+__device__ __forceinline__ bool slot_of(int s, int i, int len, int c,
+                                        const int32_t* __restrict__ bt, int64_t bt_stride,
+                                        int maxb, int num_blocks, int block_size, int& phys,
+                                        int& off) {
   const int pos = c + i;
   if (c < 0) {
     set_error(kErrPosition);
@@ -52,18 +40,69 @@ __device__ __forceinline__ bool token_slot(int t, const int32_t* __restrict__ cu
   return true;
 }
 
+// Slot of new token `t` (global token index): its sequence from cu_seqlens
+// (prefill) or t itself (decode, cu == nullptr), then slot_of.
+__device__ __forceinline__ bool token_slot(int t, const int32_t* __restrict__ cu,
+                                           const int32_t* __restrict__ ctx, int num_seqs,
+                                           const int32_t* __restrict__ bt, int64_t bt_stride,
+                                           int maxb, int num_blocks, int block_size, int& phys,
+                                           int& off) {
+  int s, i, len;
+  if (cu) {
+    s = seq_of_token(cu, num_seqs, t);
+    const int c0 = __ldg(cu + s);
+    i = t - c0;
+    len = __ldg(cu + s + 1) - c0;
+  } else {
+    s = t;
+    i = 0;
+    len = 1;
+  }
+  return slot_of(s, i, len, __ldg(ctx + s), bt, bt_stride, maxb, num_blocks, block_size, phys,
+                 off);
+}
+
 constexpr int kMaxTokPerCta = 64;
 
-// Slots of this CTA's tokens [t0, t0 + nt) into shared memory, one thread per
-// token (phys = -1: the token is not written).  Computing them once per token
-// instead of once per 16-byte vector keeps the dependent index loads
-// (cu_seqlens search, context_lens, block table) off the copy threads.
+constexpr int kSmemSeqs = 1024;  // cu_seqlens / context_lens staged in shared memory up to this
+
+// Slots of this CTA's tokens [t0, t0 + nt) into shared memory (phys = -1:
+// the token is not written), computed once per token instead of once per
+// 16-byte vector.  For prefill batches of up to kSmemSeqs sequences the CTA
+// first stages cu_seqlens and context_lens in shared memory (one cooperative
+// round trip) and searches there, so a token's slot costs two dependent
+// global loads (that stage, then its block-table entry) instead of a binary
+// search through global memory.  kStage = false skips the staging (CTAs of a
+// single token, where the stage costs more than the search).
+template <bool kStage>
 __device__ __forceinline__ void cta_token_slots(int t0, int nt, const int32_t* __restrict__ cu,
                                                 const int32_t* __restrict__ ctx, int num_seqs,
                                                 const int32_t* __restrict__ bt,
                                                 int64_t bt_stride, int maxb, int num_blocks,
                                                 int block_size, int* s_phys, int* s_off) {
-  if (threadIdx.x < nt) {
+  __shared__ int s_cu[kSmemSeqs + 1];
+  __shared__ int s_ctx[kSmemSeqs];
+  if (kStage && cu != nullptr && num_seqs <= kSmemSeqs) {  // uniform over the CTA
+    for (int i = threadIdx.x; i <= num_seqs; i += blockDim.x) {
+      s_cu[i] = __ldg(cu + i);
+      if (i < num_seqs) s_ctx[i] = __ldg(ctx + i);
+    }
+    __syncthreads();
+    if (threadIdx.x < nt) {
+      const int t = t0 + threadIdx.x;
+      int lo = 0, hi = num_seqs - 1;  // last sequence whose start is <= t
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_cu[mid] <= t) lo = mid; else hi = mid - 1;
+      }
+      int phys = -1, off = 0;
+      if (!slot_of(lo, t - s_cu[lo], s_cu[lo + 1] - s_cu[lo], s_ctx[lo], bt, bt_stride, maxb,
+                   num_blocks, block_size, phys, off))
+        phys = -1;
+      s_phys[threadIdx.x] = phys;
+      s_off[threadIdx.x] = off;
+    }
+  } else if (threadIdx.x < nt) {
     int phys = -1, off = 0;
     if (!token_slot(t0 + threadIdx.x, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks,
                     block_size, phys, off))
@@ -130,7 +169,7 @@ __global__ void __launch_bounds__(256)
     }
   };
   load(threadIdx.x);
-  cta_token_slots(t0, nt, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, s_phys,
+  cta_token_slots<true>(t0, nt, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, s_phys,
                   s_off);
   store(threadIdx.x);
   for (int base = threadIdx.x + U * blockDim.x; base < items; base += U * blockDim.x) {
@@ -352,7 +391,7 @@ __global__ void __launch_bounds__(256)
     }
   };
   load(threadIdx.x);
-  cta_token_slots(t0, nt, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, s_phys,
+  cta_token_slots<false>(t0, nt, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, s_phys,
                   s_off);
   store(threadIdx.x);
   for (int base = threadIdx.x + U * blockDim.x; base < items; base += U * blockDim.x) {
