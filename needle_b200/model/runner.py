@@ -12,9 +12,10 @@ with the mirrors in ``needle_b200.model.sequence``.
 
 Differences, all below the API: the model is materialised directly on the
 device (no CPU copy of the weights); host-built step inputs are copied from
-pinned memory without a blocking sync; greedy sampling is one batched
-argmax with a single device-to-host read (needle reads one ``int(argmax)``
-per sequence, ``needle/model/sampler.py:27-28``).
+pinned memory without a blocking sync; sampling is batched over the whole
+step with a single device-to-host read of the token ids (needle reads one
+``int(...)`` per sequence, ``needle/model/sampler.py:24-48``; see
+``needle_b200.model.sampler``).
 """
 from __future__ import annotations
 
@@ -30,6 +31,7 @@ from ..layers.rope import RotaryEmbedding
 from .config import ModelConfig
 from .llama import LlamaForCausalLM
 from .qwen2 import Qwen2ForCausalLM
+from .sampler import Sampler
 from .sequence import ExecuteInput, ExecuteOutput, SchedulerOutput
 
 
@@ -41,41 +43,6 @@ def build_model(config: ModelConfig, tp_size: int = 1, tp_rank: int = 0):
     if mt == "qwen2":
         return Qwen2ForCausalLM(config, tp_size=tp_size, tp_rank=tp_rank)
     raise ValueError(f"Unsupported model_type: {mt!r}")
-
-
-class Sampler:
-    """Top-k / top-p / temperature sampling (``needle/model/sampler.py:13-48``).
-
-    Rows with temperature 0 take one batched argmax and one host read; other
-    rows follow needle's per-row recipe.
-    """
-
-    @torch.no_grad()
-    def sample(self, logits: torch.Tensor, params_list) -> List[int]:
-        assert logits.shape[0] == len(params_list)
-        greedy = [p.temperature == 0.0 for p in params_list]
-        out: List[Optional[int]] = [None] * len(params_list)
-        if any(greedy):
-            ids = logits.argmax(dim=-1).tolist()
-            for i, g in enumerate(greedy):
-                if g:
-                    out[i] = ids[i]
-        for i, p in enumerate(params_list):
-            if greedy[i]:
-                continue
-            logit = logits[i] / p.temperature
-            if p.top_k > 0:
-                k = min(p.top_k, logit.size(-1))
-                kth = logit.topk(k).values[-1]
-                logit = logit.masked_fill(logit < kth, float("-inf"))
-            if p.top_p < 1.0:
-                sl, si = logit.sort(descending=True)
-                probs = sl.softmax(dim=-1)
-                remove = probs.cumsum(dim=-1) - probs > p.top_p
-                sl[remove] = float("-inf")
-                logit = logit.scatter(0, si, sl)
-            out[i] = int(torch.multinomial(F.softmax(logit, dim=-1), num_samples=1))
-        return out  # type: ignore[return-value]
 
 
 class _DecodeGraph:

@@ -242,3 +242,26 @@ def add_rms_norm(x, residual, weight, eps):
 def default_scale(head_dim: int) -> float:
     """Softmax scale used by needle (``needle/layers/attention.py:48``)."""
     return 1.0 / math.sqrt(head_dim)
+
+
+def sampler_filtered_logits(logit: torch.Tensor, temperature: float, top_k: int,
+                            top_p: float) -> torch.Tensor:
+    """One row of needle's sampler before the draw (``needle/model/sampler.py:33-46``).
+
+    ``logit / temperature`` with a Python float (fp32 divide, one rounding to
+    the row's dtype), top-k masking ``logit < kth`` -> -inf, then top-p on the
+    descending sort: a token is removed when the probability mass before it
+    exceeds ``top_p`` (compared in the row's dtype), scattered back.
+    """
+    logit = logit / temperature
+    if top_k > 0:
+        k = min(top_k, logit.size(-1))
+        kth = logit.topk(k).values[-1]
+        logit = logit.masked_fill(logit < kth, float("-inf"))
+    if top_p < 1.0:
+        sl, si = logit.sort(descending=True)
+        cum = sl.softmax(dim=-1).cumsum(dim=-1)
+        remove = cum - sl.softmax(dim=-1) > top_p
+        sl[remove] = float("-inf")
+        logit = logit.scatter(0, si, sl)
+    return logit

@@ -23,6 +23,11 @@ PREFILL_LENS = [1, 7, 40, 70]
 KV_WRITE_SHAPES = [(2, 64), (3, 128)]
 ROPE_SHAPES = [(14, 2, 64, 1e6), (16, 4, 128, 5e5)]
 NORM_SHAPES = [(896, 1e-6), (4096, 1e-5)]
+# (temperature, top_k, top_p) per row of the sampler case; temperature 0 = greedy
+SAMPLER_PARAMS = [(0.0, -1, 1.0), (0.7, 50, 1.0), (1.0, -1, 0.9), (1.3, 5, 0.5),
+                  (0.5, 0, 0.95), (2.0, 2000, 0.3), (0.9, 1, 1.0), (0.0, 10, 0.5),
+                  (1.0, -1, 1.0), (0.37, 17, 0.8)]
+SAMPLER_VOCAB = 1000
 
 
 def crc(*tensors) -> int:
@@ -108,3 +113,11 @@ def norm_inputs(dt: str, hid: int):
     x = (torch.randn(T, hid, generator=g) * 3).to(DTYPES[dt])
     res = (torch.randn(T, hid, generator=g) * 3).to(DTYPES[dt])
     return dict(x=x, residual=res, weight=w)
+
+
+def sampler_inputs(dt: str):
+    """Logits ``[rows, vocab]`` for the sampler case, with a block of ties."""
+    g = torch.Generator().manual_seed(606)
+    logits = (3 * torch.randn(len(SAMPLER_PARAMS), SAMPLER_VOCAB, generator=g)).to(DTYPES[dt])
+    logits[3, 10:20] = logits[3, 10]
+    return {"logits": logits}

@@ -8,7 +8,8 @@ script in the repository that imports needle):
 It runs needle's OWN code on CPU -- ``Attention._decode`` and
 ``Attention._prefill`` (KV write + attention), ``_write_kv``,
 ``_apply_rope`` with ``RotaryEmbedding`` tables, ``RMSNorm`` with the
-decoder's residual add, and for the end-to-end case ``LLMEngine.step`` over
+decoder's residual add, ``Sampler.sample`` (the probabilities it hands to
+``torch.multinomial``, captured), and for the end-to-end case ``LLMEngine.step`` over
 ``Scheduler`` / ``BlockAllocator`` / ``ModelRunner`` -- on the seeded inputs of
 ``cases.py`` and stores needle's outputs next to this file as ``.npz``.
 
@@ -143,6 +144,36 @@ def norm_cases(RMSNorm):
     return out
 
 
+def sampler_cases(src):
+    """needle's ``Sampler.sample`` on seeded logits: the greedy ids and, for
+    every sampled row, the probability vector it passes to
+    ``torch.multinomial`` (captured by wrapping that function)."""
+    sys.path.insert(0, src)
+    from needle.model.sampler import Sampler
+    from needle.backend.sequence import SamplingParams
+    out = {}
+    for dt in ("bfloat16", "float32"):
+        x = C.sampler_inputs(dt)
+        params = [SamplingParams(temperature=t, top_k=k, top_p=p) for t, k, p in C.SAMPLER_PARAMS]
+        seen = []
+        real = torch.multinomial
+
+        def capture(probs, num_samples, *a, **kw):
+            seen.append(probs.clone())
+            return real(probs, num_samples, *a, **kw)
+        torch.multinomial = capture
+        try:
+            ids = Sampler().sample(x["logits"], params)
+        finally:
+            torch.multinomial = real
+        greedy = [i for i, (t, _, _) in enumerate(C.SAMPLER_PARAMS) if t == 0.0]
+        out[f"sampler_{dt}"] = dict(input_crc=torch.tensor(C.crc(*x.values())),
+                                    greedy_rows=torch.tensor(greedy),
+                                    greedy_ids=torch.tensor([ids[i] for i in greedy]),
+                                    probs=torch.stack(seen))
+    return out
+
+
 def e2e_config1(num_prompts=8, prompt_len=128, new_tokens=65):
     """Config 1: Qwen2-0.5B shape, fp32, synthetic seed-0 weights, 8 x 128
     prompt ids, 65 greedy tokens (one from the prefill, then 64 decode steps),
@@ -203,16 +234,27 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--needle-src", required=True, help="path of a needle checkout")
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--only", default=None, help="regenerate one fixture file (e.g. sampler)")
     args = ap.parse_args()
     torch.set_num_threads(os.cpu_count() or 1)
     A, RotaryEmbedding, RMSNorm, ModelConfig = _needle(args.needle_src)
+    if args.only == "sampler":
+        with open(os.path.join(HERE, "MANIFEST.json")) as f:
+            meta = json.load(f)
+        cases = sampler_cases(args.needle_src)
+        np.savez_compressed(os.path.join(HERE, "sampler.npz"), **pack(cases))
+        meta["sampler"] = sorted(cases)
+        with open(os.path.join(HERE, "MANIFEST.json"), "w") as f:
+            json.dump(meta, f, indent=1, sort_keys=True)
+        return
     meta = {}
     with torch.no_grad():
         for name, cases in (("kv_write", kv_write_cases(A)),
                             ("decode", decode_cases(A, ModelConfig)),
                             ("prefill", prefill_cases(A, ModelConfig)),
                             ("rope", rope_cases(A, RotaryEmbedding)),
-                            ("norm", norm_cases(RMSNorm))):
+                            ("norm", norm_cases(RMSNorm)),
+                            ("sampler", sampler_cases(args.needle_src))):
             np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **pack(cases))
             meta[name] = sorted(cases)
         if not args.skip_e2e:
