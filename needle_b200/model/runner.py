@@ -19,6 +19,7 @@ step with a single device-to-host read of the token ids (needle reads one
 """
 from __future__ import annotations
 
+import itertools
 import os
 from typing import Dict, List, Optional
 
@@ -337,11 +338,14 @@ class ModelRunner:
             pos = np.asarray(pos_l, dtype=np.int64)
             max_seqlen = int((cu[1:] - cu[:-1]).max()) if B else 1
         tables = [block_tables.get(s.seq_id, []) for s in all_seqs]
-        maxb = max(1, max(map(len, tables), default=1))
+        lens = np.fromiter(map(len, tables), np.int64, B)
+        maxb = max(1, int(lens.max()) if B else 1)
         bt = np.full((B, maxb), self.padding_block, dtype=np.int32)
-        for i, t in enumerate(tables):
-            if t:
-                bt[i, :len(t)] = t
+        if B:
+            # one pass over all block ids in C, then a masked scatter into the
+            # padded table (needle's scheduler hands over fresh lists each step)
+            flat = np.fromiter(itertools.chain.from_iterable(tables), np.int32, int(lens.sum()))
+            bt[np.arange(maxb)[None, :] < lens[:, None]] = flat
         return ExecuteInput(input_ids=self._h2d(ids), position_ids=self._h2d(pos),
                             cu_seqlens=self._h2d(cu), max_seqlen=max_seqlen,
                             block_table=self._h2d(bt), context_lens=self._h2d(ctx),
