@@ -80,15 +80,19 @@ class TPComm:
         dist.all_gather_object(entries, (bytes(handle), offset.value), group=group)
         self._opened: List[int] = []
         bases = []
-        for p, (h, off) in enumerate(entries):
-            if p == self.rank:
-                bases.append(self._buf.data_ptr())
-                continue
-            hb = (ctypes.c_char * 64).from_buffer_copy(h)
-            ptr = ctypes.c_void_p(0)
-            L.check(lib.nb_ipc_open(ctypes.addressof(hb), ctypes.addressof(ptr)))
-            self._opened.append(ptr.value)
-            bases.append(ptr.value + off)
+        try:
+            for p, (h, off) in enumerate(entries):
+                if p == self.rank:
+                    bases.append(self._buf.data_ptr())
+                    continue
+                hb = (ctypes.c_char * 64).from_buffer_copy(h)
+                ptr = ctypes.c_void_p(0)
+                L.check(lib.nb_ipc_open(ctypes.addressof(hb), ctypes.addressof(ptr)))
+                self._opened.append(ptr.value)
+                bases.append(ptr.value + off)
+        except Exception:
+            self.close()  # unmap what was mapped before the failure
+            raise
         W = self.world
         self._recv = (ctypes.c_void_p * W)(*bases)
         self._gather = (ctypes.c_void_p * W)(*[b + n_recv for b in bases])
