@@ -22,8 +22,8 @@ class _HostRunner:
     padding_block = 999
     _prepare_inputs = ModelRunner._prepare_inputs
 
-    def _h2d(self, a, dtype=None):
-        return torch.from_numpy(np.ascontiguousarray(a))
+    def _h2d_many(self, arrays):
+        return [torch.from_numpy(np.ascontiguousarray(a)) for a in arrays]
 
 
 def _seq(sid, tokens, generated):
