@@ -1,4 +1,5 @@
-"""Build ``needle_b200/_lib/libneedle_b200.so`` from ``needle_b200/csrc`` with nvcc.
+"""Build ``needle_b200/_lib/libneedle_b200.so`` from ``needle_b200/csrc`` with nvcc
+(and the small host-side CPython extension ``_steppack`` with gcc).
 
 The library is a plain shared object with a C ABI (``include/needle_b200.h``);
 it does not link against torch.  It is compiled for sm_100a only and built
@@ -75,6 +76,38 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     return LIB
 
 
+HOST_SRC = os.path.join(PKG, "host", "steppack.c")
+
+
+def host_ext_path() -> str:
+    import sysconfig
+    return os.path.join(OUT_DIR, "_steppack" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_host(force: bool = False, verbose: bool = False) -> str:
+    """The CPython extension with the host-side step packing (gcc, -O2)."""
+    import sysconfig
+    out = host_ext_path()
+    stamp = out + ".srchash"
+    with open(HOST_SRC, "rb") as fh:
+        digest = hashlib.sha256(fh.read() + sys.version.encode()).hexdigest()
+    if not force and os.path.exists(out) and os.path.exists(stamp):
+        with open(stamp) as fh:
+            if fh.read().strip() == digest:
+                return out
+    os.makedirs(OUT_DIR, exist_ok=True)
+    cc = os.environ.get("CC") or shutil.which("gcc") or "cc"
+    cmd = [cc, "-O2", "-fPIC", "-shared", "-Wall", "-I", sysconfig.get_paths()["include"],
+           HOST_SRC, "-o", out + ".tmp"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(out + ".tmp", out)
+    with open(stamp, "w") as fh:
+        fh.write(digest)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -82,6 +115,7 @@ def main():
     a = ap.parse_args()
     extra = ["-Xptxas", "-v"] if a.ptxas_v else []
     print(build(force=a.force or a.ptxas_v, verbose=True, extra=extra))
+    print(build_host(force=a.force, verbose=True))
 
 
 if __name__ == "__main__":

@@ -19,7 +19,6 @@ step with a single device-to-host read of the token ids (needle reads one
 """
 from __future__ import annotations
 
-import itertools
 import os
 from typing import Dict, List, Optional
 
@@ -32,6 +31,7 @@ from ..layers.rope import RotaryEmbedding
 from .config import ModelConfig
 from .llama import LlamaForCausalLM
 from .qwen2 import Qwen2ForCausalLM
+from . import steppack
 from .sampler import Sampler
 from .sequence import ExecuteInput, ExecuteOutput, SchedulerOutput
 
@@ -69,11 +69,22 @@ class _InputStage:
         self.recorded = [False] * slots
         self.next = 0
 
-    def put(self, arrays: List[np.ndarray]) -> List[torch.Tensor]:
+    def put(self, arrays: List[np.ndarray], table=None) -> List[torch.Tensor]:
+        """Device views of ``arrays`` and, if ``table = (rows, width, pad)``
+        is given, of the padded int32 block table built from ``rows``
+        (written straight into the staging buffer by the ``_steppack``
+        extension when it is built)."""
+        if table is not None and steppack.ext() is None:
+            arrays = list(arrays) + [steppack.block_table_np(*table)]
+            table = None
         offs, total = [], 0
         for a in arrays:
             offs.append(total)
             total += -(-a.nbytes // 16) * 16
+        t_off, t_bytes = total, 0
+        if table is not None:
+            t_bytes = len(table[0]) * table[1] * 4
+            total += t_bytes
         k = self.next
         self.next = (k + 1) % len(self.host)
         if self.recorded[k]:
@@ -86,13 +97,19 @@ class _InputStage:
         hb = self.host[k].numpy()
         for a, o in zip(arrays, offs):
             hb[o:o + a.nbytes].view(a.dtype)[:] = np.ascontiguousarray(a).reshape(-1)
+        if t_bytes:
+            steppack.fill_block_table(table[0], self.host[k].data_ptr() + t_off,
+                                      self.host[k].numel() - t_off, table[1], table[2])
         db = self.dev[k]
         if total:
             db[:total].copy_(self.host[k][:total], non_blocking=True)
         self.events[k].record(torch.cuda.current_stream(self.device))
         self.recorded[k] = True
-        return [db[o:o + a.nbytes].view(self._TORCH[a.dtype]).view(a.shape)
-                for a, o in zip(arrays, offs)]
+        out = [db[o:o + a.nbytes].view(self._TORCH[a.dtype]).view(a.shape)
+               for a, o in zip(arrays, offs)]
+        if table is not None:
+            out.append(db[t_off:t_off + t_bytes].view(torch.int32).view(len(table[0]), table[1]))
+        return out
 
 
 class _DecodeGraph:
@@ -355,12 +372,13 @@ class ModelRunner:
             torch.from_numpy(data) if isinstance(data, np.ndarray) else torch.tensor(data, dtype=dtype))
         return t.pin_memory().to(self.device, non_blocking=True)
 
-    def _h2d_many(self, arrays: List[np.ndarray]) -> List[torch.Tensor]:
-        """A step's input arrays on the device with one pinned-memory copy
-        (see ``_InputStage``)."""
+    def _h2d_many(self, arrays: List[np.ndarray], table=None) -> List[torch.Tensor]:
+        """A step's input arrays (and its block table, ``table = (rows,
+        width, pad)``) on the device with one pinned-memory copy (see
+        ``_InputStage``)."""
         if self._stage is None:
             self._stage = _InputStage(self.device)
-        return self._stage.put(arrays)
+        return self._stage.put(arrays, table)
 
     def _prepare_inputs(self, prefill_seqs, decode_seqs, block_tables) -> ExecuteInput:
         """Same tensors as ``needle/model/runner.py:194-249``: a sequence with
@@ -395,15 +413,9 @@ class ModelRunner:
             pos = np.asarray(pos_l, dtype=np.int64)
             max_seqlen = int((cu[1:] - cu[:-1]).max()) if B else 1
         tables = [block_tables.get(s.seq_id, []) for s in all_seqs]
-        lens = np.fromiter(map(len, tables), np.int64, B)
-        maxb = max(1, int(lens.max()) if B else 1)
-        bt = np.full((B, maxb), self.padding_block, dtype=np.int32)
-        if B:
-            # one pass over all block ids in C, then a masked scatter into the
-            # padded table (needle's scheduler hands over fresh lists each step)
-            flat = np.fromiter(itertools.chain.from_iterable(tables), np.int32, int(lens.sum()))
-            bt[np.arange(maxb)[None, :] < lens[:, None]] = flat
-        d_ids, d_pos, d_cu, d_bt, d_ctx = self._h2d_many([ids, pos, cu, bt, ctx])
+        maxb = max(1, max(map(len, tables), default=1))
+        d_ids, d_pos, d_cu, d_ctx, d_bt = self._h2d_many([ids, pos, cu, ctx],
+                                                         table=(tables, maxb, self.padding_block))
         return ExecuteInput(input_ids=d_ids, position_ids=d_pos, cu_seqlens=d_cu,
                             max_seqlen=max_seqlen, block_table=d_bt, context_lens=d_ctx,
                             is_prefill=is_prefill)

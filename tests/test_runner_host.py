@@ -11,6 +11,7 @@ import random
 import numpy as np
 import torch
 
+from needle_b200.model import steppack
 from needle_b200.model.runner import ModelRunner
 from needle_b200.model.sequence import Request, SamplingParams, Sequence, SequenceStatus
 from oracle import model_oracle as mo
@@ -22,8 +23,11 @@ class _HostRunner:
     padding_block = 999
     _prepare_inputs = ModelRunner._prepare_inputs
 
-    def _h2d_many(self, arrays):
-        return [torch.from_numpy(np.ascontiguousarray(a)) for a in arrays]
+    def _h2d_many(self, arrays, table=None):
+        out = [torch.from_numpy(np.ascontiguousarray(a)) for a in arrays]
+        if table is not None:
+            out.append(torch.from_numpy(steppack.block_table_np(*table)))
+        return out
 
 
 def _seq(sid, tokens, generated):
@@ -73,3 +77,23 @@ def test_prepare_inputs_prefill_and_mixed():
     dec = [_seq(9, list(range(33)), 2)]
     tables[9] = [5, 6, 7]
     _check(pre, dec, tables)
+
+
+def test_steppack_extension_matches_numpy():
+    """The C packing of the block table equals the numpy one, pads, and
+    refuses rows wider than the table or buffers too small."""
+    import ctypes
+    import pytest
+    assert steppack.ext() is not None, "build the host extension: python -m needle_b200.build"
+    rnd = random.Random(2)
+    rows = [[rnd.randrange(1 << 20) for _ in range(rnd.randint(0, 70))] for _ in range(33)]
+    width = max(map(len, rows))
+    ref = steppack.block_table_np(rows, width, 12345)
+    buf = np.full(len(rows) * width + 8, -7, dtype=np.int32)
+    steppack.fill_block_table(rows, buf.ctypes.data, buf.nbytes, width, 12345)
+    assert np.array_equal(buf[:len(rows) * width].reshape(len(rows), width), ref)
+    assert (buf[len(rows) * width:] == -7).all()          # nothing written past the table
+    with pytest.raises(ValueError):
+        steppack.fill_block_table(rows, buf.ctypes.data, buf.nbytes, width - 1, 0)
+    with pytest.raises(ValueError):
+        steppack.fill_block_table(rows, buf.ctypes.data, 16, width, 0)
