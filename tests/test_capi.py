@@ -14,7 +14,9 @@ def test_header_declares_the_hot_path():
     for name in ("nb_store_kvcache", "nb_rope", "nb_rope_store_kvcache", "nb_paged_decode",
                  "nb_paged_decode_plan", "nb_paged_decode_workspace_size",
                  "nb_prefill_attention", "nb_rmsnorm", "nb_fused_add_rmsnorm",
-                 "nb_last_error", "nb_device_errors", "nb_abi_version"):
+                 "nb_last_error", "nb_device_errors", "nb_abi_version", "nb_silu_mul",
+                 "nb_swap_kv_blocks", "nb_tp_allreduce_add_rmsnorm", "nb_ipc_handle",
+                 "nb_ipc_open", "nb_ipc_close", "nb_paged_decode_noalloc"):
         assert name in decl, name
 
 
@@ -106,3 +108,60 @@ def test_bench_cpu_baseline_model_runs_on_a_tiny_config():
     r = bench.cpu_baseline_model(cfg, [5, 40, 17], 0.5)
     assert r["extrapolated"] is True and r["kind"] == "port" and r["value"] > 0
     assert "x3 layers" in r["sample"]
+
+
+def _ptrs(*vals):
+    arr = (ctypes.c_void_p * len(vals))(*vals)
+    return ctypes.cast(arr, ctypes.c_void_p), arr
+
+
+def test_tp_allreduce_arg_checks():
+    """nb_tp_allreduce_add_rmsnorm validates everything on the host."""
+    lib = L.lib()
+    recv, _r = _ptrs(4096, 8192)
+    gath, _g = _ptrs(4096 * 3, 4096 * 5)
+    ep = ctypes.cast(ctypes.c_void_p(4096 * 7), ctypes.POINTER(ctypes.c_uint))
+    f = lib.nb_tp_allreduce_add_rmsnorm
+    ok = dict(partial=4096, recv=recv, gather=gath, slot_rows=64, out=4096 * 9, res=4096 * 11,
+              epochs=ep, rank=0, world=2, weight=4096 * 13, T=64, hidden=1024, eps=1e-6,
+              dtype=L.NB_DTYPE_BF16)
+
+    def call(**kw):
+        a = dict(ok, **kw)
+        return _err(f(a["partial"], a["recv"], a["gather"], a["slot_rows"], a["out"], a["res"],
+                      a["epochs"], a["rank"], a["world"], a["weight"], a["T"], a["hidden"],
+                      a["eps"], a["dtype"], None))
+    assert call(dtype=L.NB_DTYPE_F32)[0] == L.NB_ERR_UNSUPPORTED
+    assert call(partial=None)[0] == L.NB_ERR_INVALID_ARG
+    assert call(world=9)[0] == L.NB_ERR_INVALID_ARG
+    assert call(rank=2)[0] == L.NB_ERR_INVALID_ARG
+    assert call(hidden=1028)[0] == L.NB_ERR_UNSUPPORTED
+    assert call(hidden=16384)[0] == L.NB_ERR_UNSUPPORTED
+    rc, msg = call(T=200)                          # 100 rows per rank > 64 slot rows
+    assert rc == L.NB_ERR_INVALID_ARG and "slot rows" in msg
+    rc, msg = call(T=2 * 1025, slot_rows=2048)     # more rows per rank than the kernel holds
+    assert rc == L.NB_ERR_UNSUPPORTED
+    rc, msg = call(weight=4096 + 2)
+    assert rc == L.NB_ERR_INVALID_ARG and "aligned" in msg
+    bad, _b = _ptrs(4096, 8192 + 8)
+    rc, msg = call(recv=bad)
+    assert rc == L.NB_ERR_INVALID_ARG and "aligned" in msg
+    assert call(T=0)[0] == L.NB_OK                  # nothing to do, nothing launched
+
+
+def test_ipc_and_swap_and_silu_arg_checks():
+    lib = L.lib()
+    assert _err(lib.nb_ipc_handle(None, None, None))[0] == L.NB_ERR_INVALID_ARG
+    assert _err(lib.nb_ipc_open(None, None))[0] == L.NB_ERR_INVALID_ARG
+    src, _s = _ptrs(4096)
+    dst, _d = _ptrs(8192)
+    # block bytes must be a positive multiple of 16
+    rc, msg = _err(lib.nb_swap_kv_blocks(src, dst, 1, 4096, 1, 10, 10, 100, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "multiple of 16" in msg
+    rc, msg = _err(lib.nb_swap_kv_blocks(src, dst, 0, 4096, 1, 10, 10, 128, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "num_layers" in msg
+    assert _err(lib.nb_swap_kv_blocks(src, dst, 1, 4096, 0, 10, 10, 128, None))[0] == L.NB_OK
+    rc, msg = _err(lib.nb_silu_mul(4096, 100, 8192, 64, 4, 64, L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
+    assert _err(lib.nb_silu_mul(None, 128, 8192, 64, 4, 64, L.NB_DTYPE_BF16, None))[0] == \
+        L.NB_ERR_INVALID_ARG
