@@ -139,7 +139,14 @@ class TPComm:
 
 def attach(model: torch.nn.Module, comm: Optional[TPComm]) -> None:
     """Point every ``RowParallelLinear`` without bias and every ``RMSNorm`` of
-    ``model`` at ``comm`` (``None`` detaches)."""
+    ``model`` at ``comm`` (``None`` detaches).
+
+    Contract: an attached ``RowParallelLinear`` returns its partial sums
+    un-reduced, so its output must go straight into an attached ``RMSNorm``
+    called with the residual (as in the Llama/Qwen2 decoder layers here:
+    ``o_proj`` -> ``post_attention_layernorm``, ``down_proj`` -> the next
+    ``input_layernorm`` or the final norm).  Models that use a row-parallel
+    output any other way must not be attached."""
     from .linear import RowParallelLinear
     from .norm import RMSNorm
     for m in model.modules():
