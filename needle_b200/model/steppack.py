@@ -29,10 +29,15 @@ def ext():
         from ..build import host_ext_path
         path = host_ext_path()
         if os.path.exists(path):
-            spec = importlib.util.spec_from_file_location("needle_b200._steppack", path)
-            mod = importlib.util.module_from_spec(spec)
-            spec.loader.exec_module(mod)
-            _ext = mod
+            try:
+                spec = importlib.util.spec_from_file_location("needle_b200._steppack", path)
+                mod = importlib.util.module_from_spec(spec)
+                spec.loader.exec_module(mod)
+                _ext = mod
+            except ImportError as e:  # built for another interpreter: use the numpy table
+                import warnings
+                warnings.warn(f"needle_b200: {path} does not load ({e}); "
+                              "packing block tables with numpy")
     return _ext
 
 
