@@ -73,9 +73,12 @@ class Attention(nn.Module):
                 context_lens, max_seqlen, is_prefill, cos, sin):
         T = hidden_states.shape[0]
         H, KV, D = self.num_heads, self.num_kv_heads, self.head_dim
-        if self._qkv_w is not None:
+        # getattr: patch_needle() binds this method to needle's own Attention,
+        # which has no fused q/k/v buffer
+        qkv_w = getattr(self, "_qkv_w", None)
+        if qkv_w is not None:
             # one GEMM; q/k/v are column slices of its [T, (H + 2 KV) * D] output
-            qkv = F.linear(hidden_states, self._qkv_w, self._qkv_b)
+            qkv = F.linear(hidden_states, qkv_w, self._qkv_b)
             q = qkv[:, :H * D].view(T, H, D)
             k = qkv[:, H * D:(H + KV) * D].view(T, KV, D)
             v = qkv[:, (H + KV) * D:].view(T, KV, D)

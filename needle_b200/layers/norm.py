@@ -26,10 +26,12 @@ class RMSNorm(nn.Module):
     comm = None  # TPComm: x may be a row-parallel partial sum still to be all-reduced
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None):
-        if self.comm is not None and self.comm.is_partial(x):
+        # getattr: patch_needle() binds this method to needle's own RMSNorm
+        comm = getattr(self, "comm", None)
+        if comm is not None and comm.is_partial(x):
             if residual is None:
                 raise RuntimeError("the fused TP all-reduce needs the residual")
-            return self.comm.allreduce_add_rmsnorm(x.shape[0], residual, self.weight, self.eps)
+            return comm.allreduce_add_rmsnorm(x.shape[0], residual, self.weight, self.eps)
         if residual is None:
             return ops.rmsnorm(x, self.weight, self.eps)
         return ops.fused_add_rmsnorm(x, residual, self.weight, self.eps)

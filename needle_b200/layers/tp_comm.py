@@ -71,7 +71,12 @@ class TPComm:
         self.epochs = torch.zeros(2 * _MAX_ROWS_PER_RANK, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)  # sentinels in place before any peer can write
 
+        with torch.cuda.device(self.device):  # peer buffers are mapped into this device
+            self._map_peers(group)
+
+    def _map_peers(self, group) -> None:
         lib = L.lib()
+        n_recv = 2 * self.world * self.slot_rows * self.hidden * self.partial.element_size()
         handle = (ctypes.c_char * 64)()
         offset = ctypes.c_uint64(0)
         L.check(lib.nb_ipc_handle(self._buf.data_ptr(), ctypes.addressof(handle),
@@ -119,6 +124,8 @@ class TPComm:
             res.copy_(residual)
         if weight.dtype != self.dtype or not weight.is_contiguous():
             raise TypeError("weight must be contiguous and of the buffers' dtype")
+        if torch.cuda.current_device() != self.device.index:
+            raise ValueError(f"TPComm lives on {self.device}; make it the current device")
         stream = torch.cuda.current_stream(self.device).cuda_stream
         L.check(L.lib().nb_tp_allreduce_add_rmsnorm(
             self.partial.data_ptr(), ctypes.cast(self._recv, ctypes.c_void_p),
@@ -132,8 +139,9 @@ class TPComm:
         if self._opened:
             torch.cuda.synchronize(self.device)
             lib = L.lib()
-            for p in self._opened:
-                lib.nb_ipc_close(p)
+            with torch.cuda.device(self.device):
+                for p in self._opened:
+                    lib.nb_ipc_close(p)
             self._opened = []
 
 

@@ -249,6 +249,10 @@ class ModelRunner:
     # ------------------------------------------------------------------ step
 
     def execute(self, sched_out) -> ExecuteOutput:
+        with torch.cuda.device(self.device):  # the kernels launch on this runner's GPU
+            return self._execute(sched_out)
+
+    def _execute(self, sched_out) -> ExecuteOutput:
         if sched_out.swap_out_map and self.cpu_kv_caches:
             self._swap_kv_blocks(sched_out.swap_out_map, "gpu_to_cpu")
         if sched_out.swap_in_map and self.cpu_kv_caches:
@@ -329,6 +333,11 @@ class ModelRunner:
         call this at start-up for the batch sizes they serve."""
         if not self.cuda_graph:
             return
+        with torch.cuda.device(self.device):
+            self._capture_widths(batch_size, max_blocks_per_seq, min_blocks_per_seq)
+
+    def _capture_widths(self, batch_size: int, max_blocks_per_seq: int,
+                        min_blocks_per_seq: int) -> None:
         step = self.GRAPH_WIDTH_STEP
         lo = -(-max(1, min_blocks_per_seq) // step) * step
         hi = -(-max(1, max_blocks_per_seq) // step) * step

@@ -26,9 +26,22 @@ def _dtype(t: torch.Tensor) -> int:
 
 
 def _cuda(*ts):
+    """All tensors on one CUDA device, which is the current device (the
+    kernels launch there; a pointer into another GPU's memory must never
+    reach them)."""
+    dev = None
     for t in ts:
-        if t is not None and not t.is_cuda:
+        if t is None:
+            continue
+        if not t.is_cuda:
             raise ValueError("needle_b200 ops take CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+            if dev.index != torch.cuda.current_device():
+                raise ValueError(f"tensors are on {dev} but the current device is "
+                                 f"cuda:{torch.cuda.current_device()}")
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices ({dev} and {t.device})")
 
 
 def _stream(t: torch.Tensor) -> int:
