@@ -55,6 +55,8 @@ class TPComm:
             raise ValueError(f"hidden {hidden} must be a multiple of 8 up to {_MAX_HIDDEN}")
         self.hidden, self.dtype = hidden, dtype
         self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_tokens = min(int(max_tokens), _MAX_ROWS_PER_RANK * self.world)
         # local: partial sums (the GEMM writes here), normalised output, residual
         mk = lambda: torch.zeros(self.max_tokens, hidden, dtype=dtype, device=self.device)

@@ -138,6 +138,8 @@ class ModelRunner:
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("needle_b200 runs on CUDA devices only")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.tp_size = tensor_parallel_size
         self.tp_rank = tp_rank
         self.dtype = getattr(torch, dtype) if isinstance(dtype, str) else dtype
