@@ -25,7 +25,8 @@
 //     receives the gathered normalised rows while the first receives the
 //     residual rows, so both receive batches are in flight together.
 //   * Receive and gather buffers are double-buffered by the parity of a
-//     per-row-index call counter (epochs[role][b]).  A sender writes a buffer half
+//     per-row-index call counter (epochs[role][b]; a call without the second
+//     role advances both counters, so they never drift apart).  A sender writes a buffer half
 //     again two calls later; by then its previous call has received this
 //     rank's results of the call in between, which this rank sent after it
 //     had consumed (and reset) the half being rewritten.
@@ -264,7 +265,13 @@ __global__ void __launch_bounds__(1024)
       if (threadIdx.x == 0) set_error(kErrTimeout);
       return;
     }
-    if (threadIdx.x == 0) ep[b] = s_e + 1;
+    if (threadIdx.x == 0) {
+      ep[b] = s_e + 1;
+      // Without split, role 0 also received the normalised rows: advance the
+      // second role's counter too, so both stay in step (the owners chose the
+      // gather slot half by role 0's counter) when a later call splits.
+      if (!split) epochs[kArMaxRows + b] = s_e + 1;
+    }
   }
 }
 

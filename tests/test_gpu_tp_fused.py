@@ -31,11 +31,11 @@ EPS = 1e-6
 ROWS = [1, 7, 64, 33, 2, 64]
 
 
-def _inputs(T, call, world):
+def _inputs(T, call, world, hidden=HIDDEN):
     g = torch.Generator().manual_seed(1000 * call + T)
-    parts = [torch.randn(T, HIDDEN, generator=g).to(torch.bfloat16) for _ in range(world)]
-    res = torch.randn(T, HIDDEN, generator=g).to(torch.bfloat16)
-    w = (1 + 0.1 * torch.randn(HIDDEN, generator=g)).to(torch.bfloat16)
+    parts = [torch.randn(T, hidden, generator=g).to(torch.bfloat16) for _ in range(world)]
+    res = torch.randn(T, hidden, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
     return parts, res, w
 
 
@@ -157,6 +157,55 @@ def test_fused_allreduce_rmsnorm_matches_cpu(cuda):
             assert h_exact, (r, T, call, "residual not bit-identical")
             assert y_err <= 2e-2, (r, T, call, y_err)
             assert same, (r, T, call, "ranks disagree")
+
+
+# hidden 8192: one 1024-thread CTA per SM, so 148 resident CTAs.  200 rows over
+# 2 ranks (100 row indices) run without the second receive role, 300 rows
+# (150 indices) also loop over indices in a CTA, 16 and 7 rows split: the
+# sequence mixes all three launch shapes.
+MIXED_H = 8192
+MIXED_ROWS = [200, 16, 300, 16, 7, 200, 16]
+
+
+def _mixed_worker(rank, world, port, q):
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device(f"cuda:{rank}")
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        from needle_b200 import ops
+        from needle_b200.layers.tp_comm import TPComm
+        comm = TPComm(max(MIXED_ROWS), MIXED_H, torch.bfloat16, dev)
+        report = []
+        for call, T in enumerate(MIXED_ROWS):
+            parts, res, w = _inputs(T, call, world, MIXED_H)
+            comm.partial[:T].copy_(parts[rank])
+            out, h = comm.allreduce_add_rmsnorm(T, res.to(dev), w.to(dev), EPS)
+            y_ref, h_ref = _expected(parts, res, w)
+            report.append((T, torch.equal(h.cpu(), h_ref),
+                           float((out.cpu().float() - y_ref.float()).abs().max())))
+        torch.cuda.synchronize(dev)
+        errs = ops.device_errors()
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, (report, errs)))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
+def test_fused_allreduce_mixed_launch_shapes(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run(_mixed_worker, 2)
+    for r, (report, errs) in res.items():
+        assert errs == 0, (r, errs)
+        for T, h_exact, y_err in report:
+            assert h_exact, (r, T, "residual not bit-identical")
+            assert y_err <= 2e-2, (r, T, y_err)
 
 
 def _model_worker(rank, world, port, q):
