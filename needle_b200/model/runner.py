@@ -123,6 +123,9 @@ class _DecodeGraph:
         self.bt = torch.full((B, width), dummy, dtype=torch.int32, device=device)
         self.graph = torch.cuda.CUDAGraph()
         self.logits: Optional[torch.Tensor] = None
+        # device memory the captured kernels address but no graph-pool tensor
+        # owns (the split-K plan's workspace): held for the graph's lifetime
+        self.keepalive: List[object] = []
 
 
 class ModelRunner:
@@ -323,6 +326,11 @@ class ModelRunner:
             self._graph_pool = torch.cuda.graph_pool_handle()
         with torch.cuda.graph(g.graph, pool=self._graph_pool):
             g.logits = run()
+        # The decode layers took their split-K plan (and workspace) from the
+        # shared plan cache, which may drop entries later; the graph keeps
+        # every plan of its shape alive.
+        from .. import ops
+        g.keepalive = [p for p in ops._PLANS.values() if p.key[0] == B and p.key[4] == width]
         self._graphs[(B, width)] = g
         return g
 

@@ -184,7 +184,12 @@ _PLANS: "dict" = {}
 def decode_plan(num_seqs: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
                 max_blocks: int, block_size: int, device) -> DecodePlan:
     """A cached ``DecodePlan`` for this shape: every layer of a decode step (and
-    every step with the same batch shape) shares one plan and workspace."""
+    every step with the same batch shape) shares one plan and workspace.
+
+    The cache is cleared when it grows past 64 shapes; eager launches are
+    unaffected (a freed workspace is only reused by later work on the same
+    stream), but a CUDA graph that captured a plan's workspace must keep the
+    plan alive itself (``ModelRunner`` does)."""
     key = (num_seqs, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, str(device))
     p = _PLANS.get(key)
     if p is None:
