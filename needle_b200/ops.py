@@ -323,6 +323,9 @@ def swap_kv_blocks(src_caches, dst_caches, pairs: torch.Tensor) -> None:
             raise ValueError("caches must share dtype and [2, *, kv, bs, D] geometry")
         if not (s_.is_cuda or s_.is_pinned()) or not (d_.is_cuda or d_.is_pinned()):
             raise ValueError("caches must be device tensors or pinned host tensors")
+        for t in (s_, d_):
+            if t.is_cuda and t.device != pairs.device:
+                raise ValueError(f"device caches must be on {pairs.device} (got {t.device})")
         if not s_.is_contiguous() or not d_.is_contiguous():
             raise ValueError("caches must be contiguous")
     _cuda(pairs)
