@@ -235,17 +235,35 @@ NB_API int nb_ipc_close(void* dev_ptr);
  * three local).  recv / gather: world-long arrays of peer-mapped pointers
  * (index = rank) to each rank's receive slots [2][world][slot_rows][hidden]
  * and gather slots [2][world][slot_rows][2][hidden], filled with 0xFF bytes
- * before first use.  epochs: this rank's zero-initialised 2048 uint32
- * (device).  Every owner sums the partials in rank order, so all ranks hold
- * identical bits.  ceil(T / world) <= min(1024, slot_rows), hidden % 8 == 0
- * and <= 8192, bf16/fp16, 16-byte aligned buffers.  All ranks must make the
- * same sequence of calls.
+ * before first use.  epochs: this rank's zero-initialised
+ * NB_TP_EPOCH_WORDS uint32 (device): per-row call counters, then the
+ * communicator's status word at index NB_TP_STATUS_WORD.  host_status:
+ * NULL, or a word of pinned host memory that the kernel sets to 1 when a wait
+ * on a peer times out (the host reads it without a device sync).  After a
+ * timeout the status word is set and every later call returns without
+ * touching the buffers, until the caller refills recv/gather with 0xFF and
+ * zeroes epochs (status word included) on every rank.  Every owner sums the
+ * partials in rank order, so all ranks hold identical bits.
+ * ceil(T / world) <= min(1024, slot_rows), hidden % 8 == 0 and <= 8192,
+ * bf16/fp16, 16-byte aligned buffers.  All ranks must make the same sequence
+ * of calls.
  */
+#define NB_TP_EPOCH_WORDS 2080
+#define NB_TP_STATUS_WORD 2048
 NB_API int nb_tp_allreduce_add_rmsnorm(const void* partial, void* const* recv,
                                        void* const* gather, int slot_rows, void* out,
-                                       void* residual, unsigned* epochs, int rank, int world,
-                                       const void* weight, int num_tokens, int hidden, float eps,
-                                       int dtype, void* stream);
+                                       void* residual, unsigned* epochs, unsigned* host_status,
+                                       int rank, int world, const void* weight, int num_tokens,
+                                       int hidden, float eps, int dtype, void* stream);
+
+/*
+ * Upper bound in nanoseconds of each wait that nb_tp_allreduce_add_rmsnorm
+ * makes on a peer (0 = the default of 2 s; at most 60 s).  Read at every
+ * launch, so a captured CUDA graph keeps the value of its capture.  Part of
+ * the failure handling that replaces NCCL's timeout on needle's all-reduce
+ * (needle/layers/linear.py:92-98 relies on the process group's timeout).
+ */
+NB_API int nb_tp_set_wait_limit_ns(uint64_t ns);
 
 /*
  * SwiGLU activation over a fused gate/up projection: gate_up is [T, 2*I]

@@ -42,6 +42,7 @@ _CTYPES = {
     "float": ctypes.c_float,
     "int64_t": ctypes.c_int64,
     "size_t": ctypes.c_size_t,
+    "uint64_t": ctypes.c_uint64,
     "const char*": ctypes.c_char_p,
     "int*": ctypes.POINTER(ctypes.c_int),
     "unsigned*": ctypes.POINTER(ctypes.c_uint),

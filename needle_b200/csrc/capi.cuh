@@ -77,6 +77,31 @@ int num_sms() {
   return g_sms[d];
 }
 
+int ensure_max_smem(const void* func, int bytes, const char* what) {
+  struct Entry {
+    const void* func;
+    int device;
+    int bytes;
+  };
+  static Entry table[512];
+  static int used = 0;
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < used; ++i)
+    if (table[i].func == func && table[i].device == d && table[i].bytes >= bytes) return NB_OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return fail(NB_ERR_CUDA, "%s: shared-memory attribute: %s", what, cudaGetErrorString(e));
+  for (int i = 0; i < used; ++i)
+    if (table[i].func == func && table[i].device == d) {
+      table[i].bytes = bytes;
+      return NB_OK;
+    }
+  if (used < 512) table[used++] = Entry{func, d, bytes};
+  return NB_OK;
+}
+
 int tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t cols, uint64_t rows,
                   uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows) {
   const MapKey key{base, dtype, cols, rows, row_stride_bytes, box_cols, box_rows,
@@ -122,7 +147,7 @@ int tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t cols, 
 
 extern "C" {
 
-int nb_abi_version(void) { return 1; }
+int nb_abi_version(void) { return 2; }
 
 const char* nb_last_error(void) { return g_msg; }
 

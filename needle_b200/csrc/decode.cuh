@@ -519,14 +519,8 @@ int launch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t
   using G = nb::TcGeom<D>;
   const size_t smem =
       1024 + (size_t)WARPS * STAGES * G::kStageBytes + (size_t)WARPS * STAGES * 8;
-  static bool attr_set = false;
   auto kern = nb::paged_decode_tc_kernel<T, D, WARPS, STAGES>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return check_launch("paged_decode_tc: smem attribute");
-    attr_set = true;
-  }
+  if (int rc = ensure_max_smem((const void*)kern, (int)smem, "paged_decode_tc")) return rc;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   pdl_config(cfg, attr, dim3(max_splits, kvh, B), dim3(WARPS * 32), smem, st);
@@ -562,14 +556,8 @@ int launch_decode_simt(const void* cache, int nblk, int kvh, int bs, const void*
                        float* po, float2* pml, int max_splits, int B, cudaStream_t st) {
   constexpr int GMAX = 8;
   const size_t smem = sizeof(float) * (4 * GMAX * D + 8 * GMAX);
-  static bool attr_set = false;
   auto kern = nb::paged_decode_simt_kernel<T, D, GMAX>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return check_launch("paged_decode_simt: smem attribute");
-    attr_set = true;
-  }
+  if (int rc = ensure_max_smem((const void*)kern, (int)smem, "paged_decode_simt")) return rc;
   const int nhc = (group + GMAX - 1) / GMAX;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

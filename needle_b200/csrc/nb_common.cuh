@@ -351,6 +351,10 @@ namespace nbh {
 int fail(int code, const char* fmt, ...);   // records the message, returns code
 int check_launch(const char* what);          // cudaGetLastError -> status
 int num_sms();                               // SM count of the current device
+// Raise `func`'s dynamic shared-memory limit to `bytes` on the current device.
+// The attribute is per device, so the bookkeeping is per (kernel, device):
+// the first launch on each GPU sets it, later ones find it in a table.
+int ensure_max_smem(const void* func, int bytes, const char* what);
 // Tiled 2-D tensor map over a row-major [rows, cols] tensor, 128-byte
 // swizzle, box {box_cols, box_rows}.  Cached by (ptr, shape, dtype).
 int tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t cols, uint64_t rows,

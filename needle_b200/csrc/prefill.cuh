@@ -618,14 +618,8 @@ int launch_prefill_tc(const void* q, int64_t qs, const void* k, int64_t ks, cons
   if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
   if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
   if (rc) return rc;
-  static bool attr_set = false;
   auto kern = nb::prefill_tc_kernel<T, D>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) !=
-        cudaSuccess)
-      return check_launch("prefill_tc: smem attribute");
-    attr_set = true;
-  }
+  if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc")) return r2;
   dim3 grid((max_seqlen + 127) / 128, hq, B);
   kern<<<grid, 128, G::kSmem, st>>>(qm, km, vm, cu, group, sl2, (T*)out, os);
   return check_launch("prefill_tc");
@@ -643,14 +637,8 @@ int launch_prefill_tc2(const void* q, int64_t qs, const void* k, int64_t ks, con
   if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
   if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
   if (rc) return rc;
-  static bool attr_set = false;
   auto kern = nb::prefill_tc2_kernel<T, D>;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem) !=
-        cudaSuccess)
-      return check_launch("prefill_tc2: smem attribute");
-    attr_set = true;
-  }
+  if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc2")) return r2;
   dim3 grid((max_seqlen + 255) / 256, hq, B);
   kern<<<grid, 288, G::kSmem, st>>>(qm, km, vm, cu, group, sl2, (T*)out, os);
   return check_launch("prefill_tc2");

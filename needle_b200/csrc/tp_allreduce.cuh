@@ -5,13 +5,13 @@
 // and the decoder then adds the residual and normalises
 // (needle/model/llama.py:67-72).  This kernel does all three in one launch
 // over NVLink peer memory, as a reduce-scatter followed by an all-gather,
-// with no flags and no fences: the data is its own arrival signal.
+// with no flag words: the data is its own arrival signal.
 //
 //   * Every receive buffer starts filled with a sentinel bit pattern (0xFFFF
 //     in every 16-bit lane, a NaN) that valid data never holds: senders
 //     rewrite that one NaN pattern to another NaN (0x7FFF) before storing.
 //     A reader polls a 16-byte vector until none of its lanes is the
-//     sentinel, consumes it, and writes the sentinel back.
+//     sentinel, consumes it, and later writes the sentinel back.
 //   * Rank q owns rows [q*R, q*R+R) (R = ceil(T / world)).  CTA b of every
 //     rank handles row index b: it pushes its partial of row q*R+b into
 //     owner q's receive slot [sender][b]; as owner it waits for all world
@@ -30,10 +30,31 @@
 //     again two calls later; by then its previous call has received this
 //     rank's results of the call in between, which this rank sent after it
 //     had consumed (and reset) the half being rewritten.
-// Waits are bounded; on a timeout the kernel records NB_DEVERR_TIMEOUT and
-// returns.  Only plain 16-byte loads and stores cross NVLink.
+//
+// Memory ordering (PTX memory model, system scope).  Every access that
+// another GPU can observe is strong: pushes and sentinel resets are
+// st.relaxed.sys, polls are ld.relaxed.sys.  A thread executes
+// fence.acq_rel.sys (a) before its first push of a call, (b) after its
+// receive polls and before its gather pushes, and (c) after its gather polls
+// and resets.  Each push is therefore a release and each successful poll,
+// followed by (b) or (c), an acquire, so the hand-off "rank A resets slot X,
+// then pushes; rank B observes that push (directly, or through rank 0's
+// gather, which every rank receives for every row index), then writes X"
+// puts A's reset before B's write in X's coherence order: a late reset can
+// never overwrite new data.  Consecutive launches on one stream are ordered
+// by the stream, which carries the chain from one call to the next.
+//
+// Failure: every wait is bounded (nb_tp_set_wait_limit_ns, 2 s by default).
+// A CTA that gives up records NB_DEVERR_TIMEOUT, sets the communicator's
+// status word (device memory, epochs[kArStatusWord]) and, when given, a
+// host-visible word in pinned memory, and returns.  The slots are then in an
+// unknown state, so every later call that finds the status word set returns
+// at once without touching them: the communicator stays poisoned until the
+// host refills the buffers with the sentinel and zeroes the counters and the
+// status word on every rank (TPComm.reset()).
 #pragma once
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 
 #include "nb_common.cuh"
@@ -42,6 +63,10 @@ namespace nb {
 
 constexpr int kArMaxRanks = 8;
 constexpr int kArMaxRows = 1024;  // rows per rank (row indices b); epochs hold 2 x this
+constexpr int kArStatusWord = 2 * kArMaxRows;  // epochs[kArStatusWord]: non-zero = poisoned
+constexpr int kArEpochWords = 2 * kArMaxRows + 32;
+static_assert(kArEpochWords == NB_TP_EPOCH_WORDS && kArStatusWord == NB_TP_STATUS_WORD,
+              "the header's epoch layout");
 
 struct ArPeers {
   void* recv[kArMaxRanks];    // each rank's receive slots [2][world][slot_rows][hidden]
@@ -50,13 +75,21 @@ struct ArPeers {
 
 constexpr unsigned kArSentinel = 0xFFFFFFFFu;
 
-__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void* p) {
   uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p)
                : "memory");
   return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_v4(void* p, const uint4& v) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 __device__ __forceinline__ bool lane_is_sentinel(unsigned w) {
@@ -79,16 +112,15 @@ __device__ __forceinline__ uint4 canon(uint4 v) {
 // N vectors at base + i * stride (elements of 16-bit T), i < n: all loads in
 // flight at once; while some have not arrived, all of the missing ones are
 // loaded again together, so every pass costs one memory round trip however
-// many senders are late.  Gives up (dead = true) after kWaitLimitNs, or at
-// once if an earlier wait of this thread already gave up.  Each slot is reset
-// to the sentinel after it is read.
+// many senders are late.  Gives up (dead = true) after wait_ns, or at once if
+// an earlier wait of this thread already gave up.
 template <int N, typename T>
-__device__ __forceinline__ void gather_vecs(T* base, int64_t stride, int n, uint4 (&v)[N],
-                                            bool& dead) {
+__device__ __forceinline__ void poll_vecs(const T* base, int64_t stride, int n, uint4 (&v)[N],
+                                          bool& dead, unsigned long long wait_ns) {
   unsigned missing = 0;
 #pragma unroll
   for (int i = 0; i < N; ++i)
-    if (i < n) v[i] = ld_volatile_v4(base + i * stride);
+    if (i < n) v[i] = ld_relaxed_sys_v4(base + i * stride);
 #pragma unroll
   for (int i = 0; i < N; ++i)
     if (i < n && !arrived(v[i])) missing |= 1u << i;
@@ -97,32 +129,40 @@ __device__ __forceinline__ void gather_vecs(T* base, int64_t stride, int n, uint
     while (missing) {
 #pragma unroll
       for (int i = 0; i < N; ++i)
-        if (missing & (1u << i)) v[i] = ld_volatile_v4(base + i * stride);
+        if (missing & (1u << i)) v[i] = ld_relaxed_sys_v4(base + i * stride);
 #pragma unroll
       for (int i = 0; i < N; ++i)
         if ((missing & (1u << i)) && arrived(v[i])) missing &= ~(1u << i);
-      if (missing && globaltimer() - t0 > kWaitLimitNs) {
+      if (missing && globaltimer() - t0 > wait_ns) {
         dead = true;
         break;
       }
     }
   }
+}
+
+// Write the sentinel back into n consumed slots (strong stores: a peer's next
+// write to the slot must come after them in the slot's coherence order).
+template <int N, typename T>
+__device__ __forceinline__ void reset_vecs(T* base, int64_t stride, int n) {
   const uint4 sentinel = make_uint4(kArSentinel, kArSentinel, kArSentinel, kArSentinel);
 #pragma unroll
   for (int i = 0; i < N; ++i)
-    if (i < n) *reinterpret_cast<uint4*>(base + i * stride) = sentinel;
+    if (i < n) st_relaxed_sys_v4(base + i * stride, sentinel);
 }
 
-template <typename T, int VEC>
+template <typename T, int VEC, int MAXW>
 __global__ void __launch_bounds__(1024)
     tp_allreduce_add_rmsnorm_kernel(const __grid_constant__ ArPeers P, const T* __restrict__ partial,
                                     T* __restrict__ out, T* __restrict__ res, int slot_rows,
-                                    unsigned* __restrict__ epochs, int rank, int world,
-                                    const T* __restrict__ weight, int rows, int hidden, float eps,
-                                    int split) {
+                                    unsigned* __restrict__ epochs, unsigned* host_status,
+                                    int rank, int world, const T* __restrict__ weight, int rows,
+                                    int hidden, float eps, int split,
+                                    unsigned long long wait_ns) {
   static_assert(VEC * sizeof(T) == 16, "one 16-byte vector per thread");
+  static_assert(MAXW <= kArMaxRanks, "rank capacity");
   __shared__ float red[32];
-  __shared__ unsigned s_e;
+  __shared__ unsigned s_e, s_poison;
   const int per = (rows + world - 1) / world;
   const int nvec = hidden / VEC;
   const bool mine = threadIdx.x < nvec;  // one vector per thread (hidden <= 1024 * VEC)
@@ -137,12 +177,19 @@ __global__ void __launch_bounds__(1024)
   const int G = split ? gridDim.x >> 1 : gridDim.x;
   const int role = split && blockIdx.x >= G;
   unsigned* ep = epochs + role * kArMaxRows;  // per-role call counters
+  volatile unsigned* status = epochs + kArStatusWord;
   bool dead = false;
-  uint4 v[kArMaxRanks];
+  uint4 v[MAXW];
   // The grid is at most what fits on the GPU at once (every CTA resident), so
   // a CTA waiting on a peer never blocks the CTA that the peer waits for.
   for (int b = blockIdx.x - role * G; b < per; b += G) {
-    if (threadIdx.x == 0) s_e = ep[b];
+    if (threadIdx.x == 0) {
+      s_e = ep[b];
+      s_poison = *status;
+    }
+    // (a) release: everything before this call (earlier launches' resets
+    // included, through stream order) is ordered before this call's pushes
+    fence_acq_rel_sys();
     // owners q with a row at index b: q*per+b < rows
     const int nq = min(world, (rows - 1 - b) / per + 1);
     if (role == 0) {
@@ -150,37 +197,38 @@ __global__ void __launch_bounds__(1024)
       //    (the partial loads overlap the call-counter load)
       if (mine) {
 #pragma unroll
-        for (int q = 0; q < kArMaxRanks; ++q)
+        for (int q = 0; q < MAXW; ++q)
           if (q < nq)
             v[q] = *reinterpret_cast<const uint4*>(partial + (int64_t)(q * per + b) * hidden + col);
       }
       __syncthreads();
+      if (s_poison) return;  // poisoned by an earlier timeout: touch nothing
       const int par = s_e & 1;
       if (mine) {
 #pragma unroll
-        for (int q = 0; q < kArMaxRanks; ++q)
+        for (int q = 0; q < MAXW; ++q)
           if (q < nq)
-            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(P.recv[q]) +
-                                      ((int64_t)par * world + rank) * slot + (int64_t)b * hidden +
-                                      col) = canon(v[q]);
+            st_relaxed_sys_v4(reinterpret_cast<T*>(P.recv[q]) +
+                                  ((int64_t)par * world + rank) * slot + (int64_t)b * hidden + col,
+                              canon(v[q]));
       }
       // 2. owner of row rank*per+b: sum the world slots, residual, RMSNorm, all-gather
       const int row = rank * per + b;
       if (row < rows) {  // uniform over the CTA
         float ss = 0.f;
         T hv[VEC];
+        T* rb = reinterpret_cast<T*>(P.recv[rank]) + (int64_t)par * world * slot +
+                (int64_t)b * hidden + col;
         if (mine) {
-          T* rb = reinterpret_cast<T*>(P.recv[rank]) + (int64_t)par * world * slot +
-                  (int64_t)b * hidden + col;
           T rv[VEC];
           *reinterpret_cast<uint4*>(rv) =
               *reinterpret_cast<const uint4*>(res + (int64_t)row * hidden + col);
-          gather_vecs<kArMaxRanks>(rb, slot, world, v, dead);  // slots reset for two calls later
+          poll_vecs<MAXW>(rb, slot, world, v, dead, wait_ns);
           float acc[VEC];
 #pragma unroll
           for (int k = 0; k < VEC; ++k) acc[k] = 0.f;
 #pragma unroll
-          for (int p = 0; p < kArMaxRanks; ++p) {  // fixed rank order: identical bits everywhere
+          for (int p = 0; p < MAXW; ++p) {  // fixed rank order: identical bits everywhere
             if (p < world) {
               const T* x = reinterpret_cast<const T*>(&v[p]);
 #pragma unroll
@@ -222,47 +270,76 @@ __global__ void __launch_bounds__(1024)
           const uint4 o4 = canon(*reinterpret_cast<uint4*>(ov));
           const int64_t g =
               ((int64_t)par * world + rank) * 2 * slot + (int64_t)b * 2 * hidden + col;
+          // A thread whose wait ran out pushes nothing more, so every rank
+          // that needs its rows times out as well instead of reading garbage.
+          if (!dead) {
+            // (b) acquire the receive polls, release before the gather pushes
+            fence_acq_rel_sys();
 #pragma unroll
-          for (int p = 0; p < kArMaxRanks; ++p) {
-            if (p < world) {
-              T* gp = reinterpret_cast<T*>(P.gather[p]) + g;
-              *reinterpret_cast<uint4*>(gp) = h4;
-              *reinterpret_cast<uint4*>(gp + hidden) = o4;
+            for (int p = 0; p < MAXW; ++p) {
+              if (p < world) {
+                T* gp = reinterpret_cast<T*>(P.gather[p]) + g;
+                st_relaxed_sys_v4(gp, h4);
+                st_relaxed_sys_v4(gp + hidden, o4);
+              }
             }
+            // the consumed receive slots, reset off the critical path (they
+            // are written again two calls later, after (a) of a later launch)
+            reset_vecs<MAXW>(rb, slot, world);
           }
         }
       }
       // 3. all-gather receive, residual rows q*per+b from their owners q
-      if (mine) {
+      if (mine && !dead) {
         T* gb = reinterpret_cast<T*>(P.gather[rank]) + (int64_t)par * world * 2 * slot +
                 (int64_t)b * 2 * hidden + col;
-        gather_vecs<kArMaxRanks>(gb, 2 * slot, nq, v, dead);
+        poll_vecs<MAXW>(gb, 2 * slot, nq, v, dead, wait_ns);
+        if (!dead) {
 #pragma unroll
-        for (int q = 0; q < kArMaxRanks; ++q)
-          if (q < nq) *reinterpret_cast<uint4*>(res + (int64_t)(q * per + b) * hidden + col) = v[q];
-        if (!split) {
-          gather_vecs<kArMaxRanks>(gb + hidden, 2 * slot, nq, v, dead);
-#pragma unroll
-          for (int q = 0; q < kArMaxRanks; ++q)
+          for (int q = 0; q < MAXW; ++q)
             if (q < nq)
-              *reinterpret_cast<uint4*>(out + (int64_t)(q * per + b) * hidden + col) = v[q];
+              *reinterpret_cast<uint4*>(res + (int64_t)(q * per + b) * hidden + col) = v[q];
+          reset_vecs<MAXW>(gb, 2 * slot, nq);
+        }
+        if (!split && !dead) {
+          poll_vecs<MAXW>(gb + hidden, 2 * slot, nq, v, dead, wait_ns);
+          if (!dead) {
+#pragma unroll
+            for (int q = 0; q < MAXW; ++q)
+              if (q < nq)
+                *reinterpret_cast<uint4*>(out + (int64_t)(q * per + b) * hidden + col) = v[q];
+            reset_vecs<MAXW>(gb + hidden, 2 * slot, nq);
+          }
         }
       }
     } else {
       __syncthreads();
+      if (s_poison) return;
       const int par = s_e & 1;
       // 3'. all-gather receive, normalised rows q*per+b from their owners q
       if (mine) {
         T* gb = reinterpret_cast<T*>(P.gather[rank]) + (int64_t)par * world * 2 * slot +
                 (int64_t)b * 2 * hidden + hidden + col;
-        gather_vecs<kArMaxRanks>(gb, 2 * slot, nq, v, dead);
+        poll_vecs<MAXW>(gb, 2 * slot, nq, v, dead, wait_ns);
+        if (!dead) {
 #pragma unroll
-        for (int q = 0; q < kArMaxRanks; ++q)
-          if (q < nq) *reinterpret_cast<uint4*>(out + (int64_t)(q * per + b) * hidden + col) = v[q];
+          for (int q = 0; q < MAXW; ++q)
+            if (q < nq)
+              *reinterpret_cast<uint4*>(out + (int64_t)(q * per + b) * hidden + col) = v[q];
+          reset_vecs<MAXW>(gb, 2 * slot, nq);
+        }
       }
     }
+    // (c) acquire the gather polls: what a peer did before its gather push is
+    // ordered before this rank's next pushes
+    fence_acq_rel_sys();
     if (__syncthreads_or(dead)) {
-      if (threadIdx.x == 0) set_error(kErrTimeout);
+      if (threadIdx.x == 0) {
+        set_error(kErrTimeout);
+        *status = 1u;
+        if (host_status) *reinterpret_cast<volatile unsigned*>(host_status) = 1u;
+        __threadfence_system();
+      }
       return;
     }
     if (threadIdx.x == 0) {
@@ -325,10 +402,21 @@ int nb_ipc_close(void* dev_ptr) {
   return NB_OK;
 }
 
+namespace {
+std::atomic<unsigned long long> g_ar_wait_ns{0};  // 0: nb::kWaitLimitNs
+}
+
+int nb_tp_set_wait_limit_ns(uint64_t ns) {
+  if (ns > 60ull * 1000000000ull)
+    return nbh::fail(NB_ERR_INVALID_ARG, "wait limit above 60 s");
+  g_ar_wait_ns.store(ns);
+  return NB_OK;
+}
+
 int nb_tp_allreduce_add_rmsnorm(const void* partial, void* const* recv, void* const* gather,
                                 int slot_rows, void* out, void* residual, unsigned* epochs,
-                                int rank, int world, const void* weight, int num_tokens,
-                                int hidden, float eps, int dtype, void* stream) {
+                                unsigned* host_status, int rank, int world, const void* weight,
+                                int num_tokens, int hidden, float eps, int dtype, void* stream) {
   using namespace nbh;
   if (!valid_dtype(dtype) || dtype == NB_DTYPE_F32)
     return fail(NB_ERR_UNSUPPORTED, "fused TP all-reduce supports bf16/fp16");
@@ -367,13 +455,25 @@ int nb_tp_allreduce_add_rmsnorm(const void* partial, void* const* recv, void* co
     const int cap = occ * num_sms();
     const int split = 2 * per <= cap;
     const int grid = split ? 2 * per : std::min(per, cap);
+    const unsigned long long w = g_ar_wait_ns.load();
     kern<<<grid, threads, 0, st>>>(P, (const T*)partial, (T*)out, (T*)residual, slot_rows, epochs,
-                                   rank, world, (const T*)weight, num_tokens, hidden, eps, split);
+                                   host_status, rank, world, (const T*)weight, num_tokens, hidden,
+                                   eps, split, w ? w : nb::kWaitLimitNs);
     return check_launch("tp_allreduce_add_rmsnorm");
   };
-  if (dtype == NB_DTYPE_BF16)
-    return launch(nb::tp_allreduce_add_rmsnorm_kernel<__nv_bfloat16, 8>, (__nv_bfloat16*)nullptr);
-  return launch(nb::tp_allreduce_add_rmsnorm_kernel<__half, 8>, (__half*)nullptr);
+  // per-thread vector arrays sized for the group: fewer registers below 8 ranks
+#define NB_AR_LAUNCH(W)                                                                      \
+  if (world <= W) {                                                                          \
+    if (dtype == NB_DTYPE_BF16)                                                              \
+      return launch(nb::tp_allreduce_add_rmsnorm_kernel<__nv_bfloat16, 8, W>,                \
+                    (__nv_bfloat16*)nullptr);                                                \
+    return launch(nb::tp_allreduce_add_rmsnorm_kernel<__half, 8, W>, (__half*)nullptr);      \
+  }
+  NB_AR_LAUNCH(2)
+  NB_AR_LAUNCH(4)
+  NB_AR_LAUNCH(8)
+#undef NB_AR_LAUNCH
+  return fail(NB_ERR_INVALID_ARG, "world %d", world);
 }
 
 }  // extern "C"

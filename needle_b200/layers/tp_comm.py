@@ -16,6 +16,13 @@ launches the fused kernel, so the sequence of modules (and needle's module
 API) is unchanged.  All pointers are fixed for the life of the object, so the
 launches can be captured in CUDA graphs.  Calls with more tokens than the
 buffers hold fall back to NCCL.
+
+Failure: every wait of the kernel on a peer is bounded (2 s by default,
+``set_wait_limit``).  A kernel that gives up marks the communicator poisoned
+in device memory (later launches, graph replays included, return without
+touching the buffers) and in a pinned host word that ``check()`` reads with
+no device sync.  A poisoned ``TPComm`` refuses further calls (``TPCommError``)
+until every rank calls ``reset()``, which refills the buffers and counters.
 """
 from __future__ import annotations
 
@@ -31,6 +38,19 @@ _MAX_ROWS_PER_RANK = 1024
 _MAX_WORLD = 8
 _MAX_HIDDEN = 8192
 _SEGMENT = 2 << 20                  # whole allocator segments: nothing else shares the mapping
+_EPOCH_WORDS = 2080                 # NB_TP_EPOCH_WORDS: 2 x 1024 call counters + status word
+_STATUS_WORD = 2048                 # NB_TP_STATUS_WORD
+
+
+class TPCommError(RuntimeError):
+    """A wait on a peer timed out; the communicator is poisoned until reset()."""
+
+
+def set_wait_limit(seconds: float) -> None:
+    """Bound of every wait of the fused kernel on a peer (process-wide; 0
+    restores the default of 2 s).  Launches read it, so graphs keep the value
+    they were captured with."""
+    L.check(L.lib().nb_tp_set_wait_limit_ns(int(seconds * 1e9)))
 
 
 class TPComm:
@@ -69,8 +89,11 @@ class TPComm:
         n_gather = 2 * n_recv
         total = -(-(n_recv + n_gather) // _SEGMENT) * _SEGMENT
         self._buf = torch.full((total,), 0xFF, dtype=torch.uint8, device=self.device)
-        # per-row-index call counters of the kernel's two CTA roles
-        self.epochs = torch.zeros(2 * _MAX_ROWS_PER_RANK, dtype=torch.int32, device=self.device)
+        # per-row-index call counters of the kernel's two CTA roles, then the
+        # status word (non-zero: poisoned by a timed-out wait)
+        self.epochs = torch.zeros(_EPOCH_WORDS, dtype=torch.int32, device=self.device)
+        # host-visible copy of the status, written by the kernel over PCIe
+        self.status_host = torch.zeros(4, dtype=torch.int32, pin_memory=True)
         torch.cuda.synchronize(self.device)  # sentinels in place before any peer can write
 
         with torch.cuda.device(self.device):  # peer buffers are mapped into this device
@@ -105,7 +128,35 @@ class TPComm:
         self._gather = (ctypes.c_void_p * W)(*[b + n_recv for b in bases])
         self._epochs = ctypes.cast(ctypes.c_void_p(self.epochs.data_ptr()),
                                    ctypes.POINTER(ctypes.c_uint))
+        self._status_host = ctypes.cast(ctypes.c_void_p(self.status_host.data_ptr()),
+                                        ctypes.POINTER(ctypes.c_uint))
         dist.barrier(group=group)  # every rank has mapped every buffer
+
+    def poisoned(self) -> bool:
+        """True once a kernel of this communicator timed out (no device sync:
+        reads the pinned host word, which completed kernels have written)."""
+        return bool(self.status_host[0].item())
+
+    def check(self) -> None:
+        """Raise ``TPCommError`` if a kernel launched so far (and completed)
+        timed out waiting on a peer."""
+        if self.poisoned():
+            raise TPCommError(
+                f"fused TP all-reduce on rank {self.rank}: a wait on a peer timed out; the "
+                "communicator is poisoned until every rank calls TPComm.reset()")
+
+    def reset(self) -> None:
+        """Collective: make a poisoned communicator usable again.  Every rank
+        waits for its own work, then all refill their buffers with the
+        sentinel and zero the counters and the status, then meet again."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            self._buf.fill_(0xFF)
+            self.epochs.zero_()
+        torch.cuda.synchronize(self.device)
+        self.status_host.zero_()
+        dist.barrier(group=self.group)
 
     def can_fuse(self, num_tokens: int) -> bool:
         return 0 < num_tokens <= self.max_tokens
@@ -128,12 +179,14 @@ class TPComm:
             raise TypeError("weight must be contiguous and of the buffers' dtype")
         if torch.cuda.current_device() != self.device.index:
             raise ValueError(f"TPComm lives on {self.device}; make it the current device")
+        self.check()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         L.check(L.lib().nb_tp_allreduce_add_rmsnorm(
             self.partial.data_ptr(), ctypes.cast(self._recv, ctypes.c_void_p),
             ctypes.cast(self._gather, ctypes.c_void_p), self.slot_rows, self.out.data_ptr(),
-            self.residual.data_ptr(), self._epochs, self.rank, self.world, weight.data_ptr(), T,
-            self.hidden, float(eps), 2 if self.dtype == torch.bfloat16 else 1, stream))
+            self.residual.data_ptr(), self._epochs, self._status_host, self.rank, self.world,
+            weight.data_ptr(), T, self.hidden, float(eps),
+            2 if self.dtype == torch.bfloat16 else 1, stream))
         return self.out[:T], res
 
     def close(self) -> None:

@@ -273,8 +273,10 @@ class ModelRunner:
                                            sched_out.block_tables)
                 logits = self._forward(inp)
         params = [s.request.sampling_params for s in all_seqs]
-        return ExecuteOutput(seq_ids=[s.seq_id for s in all_seqs],
-                             next_token_ids=self.sampler.sample(logits, params))
+        ids = self.sampler.sample(logits, params)   # synchronises with the step's kernels
+        if self.tp_comm is not None:
+            self.tp_comm.check()  # a timed-out all-reduce poisons the step: raise, not bad tokens
+        return ExecuteOutput(seq_ids=[s.seq_id for s in all_seqs], next_token_ids=ids)
 
     def _forward(self, inp: ExecuteInput) -> torch.Tensor:
         if self.cuda_graph and not inp.is_prefill:

@@ -16,7 +16,8 @@ def test_header_declares_the_hot_path():
                  "nb_prefill_attention", "nb_rmsnorm", "nb_fused_add_rmsnorm",
                  "nb_last_error", "nb_device_errors", "nb_abi_version", "nb_silu_mul",
                  "nb_swap_kv_blocks", "nb_tp_allreduce_add_rmsnorm", "nb_ipc_handle",
-                 "nb_ipc_open", "nb_ipc_close", "nb_paged_decode_noalloc"):
+                 "nb_ipc_open", "nb_ipc_close", "nb_paged_decode_noalloc",
+                 "nb_tp_set_wait_limit_ns"):
         assert name in decl, name
 
 
@@ -28,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     for name in L.declared_functions():
         assert name in exported, f"{name} declared but not exported"
         assert getattr(lib, name) is not None
-    assert lib.nb_abi_version() == 1
+    assert lib.nb_abi_version() == 2
 
 
 def test_no_torch_types_in_signatures():
@@ -129,8 +130,8 @@ def test_tp_allreduce_arg_checks():
     def call(**kw):
         a = dict(ok, **kw)
         return _err(f(a["partial"], a["recv"], a["gather"], a["slot_rows"], a["out"], a["res"],
-                      a["epochs"], a["rank"], a["world"], a["weight"], a["T"], a["hidden"],
-                      a["eps"], a["dtype"], None))
+                      a["epochs"], None, a["rank"], a["world"], a["weight"], a["T"],
+                      a["hidden"], a["eps"], a["dtype"], None))
     assert call(dtype=L.NB_DTYPE_F32)[0] == L.NB_ERR_UNSUPPORTED
     assert call(partial=None)[0] == L.NB_ERR_INVALID_ARG
     assert call(world=9)[0] == L.NB_ERR_INVALID_ARG
@@ -147,6 +148,13 @@ def test_tp_allreduce_arg_checks():
     rc, msg = call(recv=bad)
     assert rc == L.NB_ERR_INVALID_ARG and "aligned" in msg
     assert call(T=0)[0] == L.NB_OK                  # nothing to do, nothing launched
+
+
+def test_tp_wait_limit_arg_checks():
+    lib = L.lib()
+    rc, msg = _err(lib.nb_tp_set_wait_limit_ns(61 * 10**9))
+    assert rc == L.NB_ERR_INVALID_ARG and "60 s" in msg
+    assert _err(lib.nb_tp_set_wait_limit_ns(0))[0] == L.NB_OK   # back to the default
 
 
 def test_ipc_and_swap_and_silu_arg_checks():

@@ -15,9 +15,12 @@ the expected result is computed on the CPU:
 
 Calls of different row counts exercise the per-row call counters and the
 double-buffered slots; a partial holding the exchange's sentinel NaN pattern
-must come out as a NaN; a CUDA graph replays the launch with new data.  The model test runs a TP=2 bf16 decode
-with the fused path and with NCCL and compares the logits.  NVLS is off for
-these multi-process runs.  Skipped with fewer than two GPUs.
+must come out as a NaN; a CUDA graph replays the launch with new data; 10^4
+calls cycle through every launch shape; a rank that skips a call makes the
+other's bounded wait run out, which poisons the communicator until a
+collective reset.  The model test runs a TP=2 bf16 decode with the fused path
+and with NCCL and compares the logits.  NVLS is off for these multi-process
+runs.  Skipped with fewer than two GPUs.
 """
 import os
 
@@ -206,6 +209,134 @@ def test_fused_allreduce_mixed_launch_shapes(cuda):
         for T, h_exact, y_err in report:
             assert h_exact, (r, T, "residual not bit-identical")
             assert y_err <= 2e-2, (r, T, y_err)
+
+
+STRESS_ROWS = [7, 16, 200, 300]   # split, split, non-split, non-split with index loops
+STRESS_CALLS = 10000
+
+
+def _stress_worker(rank, world, port, q):
+    """10^4 calls cycling through launch shapes with and without the second
+    receive role; every 997th call is checked against the CPU result."""
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device(f"cuda:{rank}")
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=dev)
+        from needle_b200 import ops
+        from needle_b200.layers.tp_comm import TPComm
+        comm = TPComm(max(STRESS_ROWS), MIXED_H, torch.bfloat16, dev)
+        sets = {}
+        for T in STRESS_ROWS:
+            parts, res, w = _inputs(T, 7, world, MIXED_H)
+            y_ref, h_ref = _expected(parts, res, w)
+            sets[T] = (parts[rank].to(dev), res.to(dev), w.to(dev), y_ref, h_ref)
+        bad = []
+        checked = 0
+        for i in range(STRESS_CALLS):
+            T = STRESS_ROWS[(i * 7 + i // 3) % len(STRESS_ROWS)]
+            part, res, w, y_ref, h_ref = sets[T]
+            comm.partial[:T].copy_(part)
+            out, h = comm.allreduce_add_rmsnorm(T, res, w, EPS)
+            if i % 997 == 0 or i == STRESS_CALLS - 1:
+                checked += 1
+                if not torch.equal(h.cpu(), h_ref) or \
+                        float((out.cpu().float() - y_ref.float()).abs().max()) > 2e-2:
+                    bad.append((i, T))
+        torch.cuda.synchronize(dev)
+        errs = ops.device_errors()
+        poisoned = comm.poisoned()
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, (bad, checked, errs, poisoned)))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
+def test_fused_allreduce_stress_mixed_shapes(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run(_stress_worker, 2)
+    for r, (bad, checked, errs, poisoned) in res.items():
+        assert errs == 0 and not poisoned, (r, errs)
+        assert checked >= 10 and not bad, (r, bad)
+
+
+def _poison_worker(rank, world, port, q):
+    """Rank 1 skips one call.  Rank 0's wait on it runs out (0.2 s limit):
+    the kernel reports NB_DEVERR_TIMEOUT, the communicator is poisoned and
+    refuses the next call on the host.  Rank 1's next call then also times
+    out.  After TPComm.reset() on both ranks a call is exact again."""
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device(f"cuda:{rank}")
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        from needle_b200 import ops
+        from needle_b200.layers.tp_comm import TPComm, TPCommError, set_wait_limit
+        set_wait_limit(0.2)
+        comm = TPComm(64, HIDDEN, torch.bfloat16, dev)
+        log = {}
+
+        def call(T, seed):
+            parts, res, w = _inputs(T, seed, world)
+            comm.partial[:T].copy_(parts[rank])
+            out, h = comm.allreduce_add_rmsnorm(T, res.to(dev), w.to(dev), EPS)
+            torch.cuda.synchronize(dev)
+            y_ref, h_ref = _expected(parts, res, w)
+            return torch.equal(h.cpu(), h_ref) and \
+                float((out.cpu().float() - y_ref.float()).abs().max()) <= 2e-2
+
+        log["good_before"] = call(16, 1)
+        log["errs_before"] = ops.device_errors()
+        dist.barrier()
+        if rank == 0:
+            call(16, 2)                         # rank 1 never makes this call
+            log["poisoned_after_skip"] = comm.poisoned()
+            log["errs_after_skip"] = ops.device_errors()
+        dist.barrier()
+        try:
+            call(16, 3)
+            log["next_call"] = "ran"
+        except TPCommError:
+            log["next_call"] = "refused"
+        log["poisoned_end"] = comm.poisoned()
+        log["errs_end"] = ops.device_errors()
+        comm.reset()
+        log["poisoned_after_reset"] = comm.poisoned()
+        log["good_after_reset"] = call(16, 4) and call(48, 5)
+        log["errs_after_reset"] = ops.device_errors()
+        set_wait_limit(0)
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, log))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
+def test_fused_allreduce_timeout_poisons_until_reset(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    TIMEOUT = 4  # NB_DEVERR_TIMEOUT
+    res = _run(_poison_worker, 2)
+    r0, r1 = res[0], res[1]
+    for log in (r0, r1):
+        assert log["good_before"] and log["errs_before"] == 0, log
+        assert log["poisoned_end"], log
+        assert log["errs_end"] & TIMEOUT or log.get("errs_after_skip", 0) & TIMEOUT, log
+        assert not log["poisoned_after_reset"], log
+        assert log["good_after_reset"] and log["errs_after_reset"] == 0, log
+    assert r0["poisoned_after_skip"] and r0["errs_after_skip"] & TIMEOUT, r0
+    assert r0["next_call"] == "refused", r0      # refused on the host, nothing launched
+    assert r1["next_call"] == "ran", r1          # launched, timed out on the device
 
 
 def _model_worker(rank, world, port, q):
