@@ -318,9 +318,19 @@ def swap_kv_blocks(src_caches, dst_caches, pairs: torch.Tensor) -> None:
     import ctypes
     if len(src_caches) != len(dst_caches) or not src_caches:
         raise ValueError("src/dst cache lists must be non-empty and of equal length")
+    # one block size and one block count per side: the kernel addresses every
+    # layer with layer 0's geometry (V half at num_blocks * block_bytes)
+    s0, d0 = src_caches[0], dst_caches[0]
     for s_, d_ in zip(src_caches, dst_caches):
-        if s_.dtype != d_.dtype or s_.shape[0] != 2 or s_.shape[2:] != d_.shape[2:]:
+        if s_.dtype != d_.dtype or s_.dim() != 5 or s_.shape[0] != 2 or s_.shape[2:] != d_.shape[2:]:
             raise ValueError("caches must share dtype and [2, *, kv, bs, D] geometry")
+        if s_.shape != s0.shape or s_.dtype != s0.dtype:
+            raise ValueError(f"every source cache must have shape {tuple(s0.shape)} and dtype "
+                             f"{s0.dtype} (got {tuple(s_.shape)}, {s_.dtype})")
+        if d_.shape != d0.shape or d_.dtype != d0.dtype:
+            raise ValueError(f"every destination cache must have shape {tuple(d0.shape)} and "
+                             f"dtype {d0.dtype} (got {tuple(d_.shape)}, {d_.dtype})")
+    for s_, d_ in zip(src_caches, dst_caches):
         if not (s_.is_cuda or s_.is_pinned()) or not (d_.is_cuda or d_.is_pinned()):
             raise ValueError("caches must be device tensors or pinned host tensors")
         for t in (s_, d_):

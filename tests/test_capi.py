@@ -173,3 +173,18 @@ def test_ipc_and_swap_and_silu_arg_checks():
     assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
     assert _err(lib.nb_silu_mul(None, 128, 8192, 64, 4, 64, L.NB_DTYPE_BF16, None))[0] == \
         L.NB_ERR_INVALID_ARG
+
+
+def test_swap_wrapper_rejects_mixed_layer_geometry():
+    """Every layer is addressed with layer 0's block count and block size, so
+    a layer of another shape is rejected before anything reaches the device."""
+    import torch
+    from needle_b200 import ops
+    a = torch.zeros(2, 8, 2, 16, 64, dtype=torch.bfloat16)
+    b = torch.zeros(2, 9, 2, 16, 64, dtype=torch.bfloat16)        # another block count
+    d = torch.zeros(2, 8, 2, 16, 64, dtype=torch.bfloat16)
+    pairs = torch.zeros(1, 2, dtype=torch.int32)
+    with pytest.raises(ValueError, match="every source cache"):
+        ops.swap_kv_blocks([a, b], [d, d], pairs)
+    with pytest.raises(ValueError, match="every destination cache"):
+        ops.swap_kv_blocks([a, a], [d, b], pairs)
