@@ -81,6 +81,51 @@ NB_API int nb_store_kvcache(const void* k, int64_t k_stride, const void* v, int6
                      void* stream);
 
 /*
+ * Slot table of one forward: slots[t] = block * block_size + offset of new
+ * token t in the paged cache, or -1 when the token is not written (a block id
+ * outside [0, num_blocks) or a negative context length, both recorded in the
+ * device error word; or an earlier token on a clamped slot that a later token
+ * of the same sequence overwrites).  Same index math, clamp and
+ * last-token-wins rule as nb_store_kvcache, which restates
+ * needle/layers/attention.py:214-240 (prefill) and :140-154 (decode).
+ * needle recomputes these positions in every layer; here the table is built
+ * once per forward and read by every layer's nb_store_kvcache_slots /
+ * nb_rope_store_kvcache_slots.  cu_seqlens == NULL: one token per sequence.
+ */
+NB_API int nb_slot_mapping(const int32_t* block_table, int64_t block_table_stride,
+                           int max_blocks_per_seq, const int32_t* cu_seqlens,
+                           const int32_t* context_lens, int num_seqs, int num_tokens,
+                           int block_size, int num_blocks, int32_t* slots, void* stream);
+
+/*
+ * nb_store_kvcache with the positions taken from a slot table
+ * (nb_slot_mapping): token t's K/V rows go to block slots[t] / block_size,
+ * row slots[t] % block_size; slots[t] < 0 is skipped.  Replaces
+ * needle/layers/attention.py:140-154 and :204-246 like nb_store_kvcache.
+ * Rows must be 16-byte aligned.  Byte-exact copy.
+ */
+NB_API int nb_store_kvcache_slots(const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                                  void* kv_cache, int num_blocks, int num_kv_heads,
+                                  int block_size, int head_dim, const int32_t* slots,
+                                  int num_tokens, int dtype, void* stream);
+
+/*
+ * nb_rope_store_kvcache with the positions taken from a slot table: q is
+ * rotated in place, k rotated and written to the cache (and back into k when
+ * write_k_back != 0), v copied to the cache.  Replaces
+ * needle/layers/attention.py:88 (_apply_rope) + :140-154 or :204-246.  Same
+ * rounding as nb_rope (bit-identical to the reference).  Rows must be
+ * 16-byte aligned.
+ */
+NB_API int nb_rope_store_kvcache_slots(void* q, int64_t q_stride, int num_q_heads, void* k,
+                                       int64_t k_stride, const void* v, int64_t v_stride,
+                                       const void* cos, const void* sin, int64_t cs_stride,
+                                       void* kv_cache, int num_blocks, int num_kv_heads,
+                                       int block_size, int head_dim, const int32_t* slots,
+                                       int num_tokens, int write_k_back, int dtype,
+                                       void* stream);
+
+/*
  * In-place NeoX rotary embedding of q [T, num_q_heads, D] and k
  * [T, num_kv_heads, D] with per-token tables cos/sin [T, D] (row stride
  * cs_stride).  Replaces needle/layers/attention.py:277-288 (_apply_rope):

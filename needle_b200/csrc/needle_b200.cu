@@ -5,6 +5,7 @@
 
 #include "capi.cuh"
 #include "kvcache.cuh"
+#include "slots.cuh"
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "norm.cuh"

@@ -91,6 +91,19 @@ __device__ __forceinline__ void st_relaxed_sys_v4(void* p, const uint4& v) {
 __device__ __forceinline__ void fence_acq_rel_sys() {
   asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
+#ifndef NB_AR_FENCE_MASK
+#define NB_AR_FENCE_MASK 7
+#endif
+#ifndef NB_AR_FENCE_GPU
+#define NB_AR_FENCE_GPU 0
+#endif
+template <int BIT>
+__device__ __forceinline__ void ar_fence() {
+  if constexpr ((NB_AR_FENCE_MASK & BIT) != 0) {
+    if constexpr (NB_AR_FENCE_GPU) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    else fence_acq_rel_sys();
+  }
+}
 
 __device__ __forceinline__ bool lane_is_sentinel(unsigned w) {
   return (w & 0xFFFFu) == 0xFFFFu || (w >> 16) == 0xFFFFu;
@@ -189,7 +202,7 @@ __global__ void __launch_bounds__(1024)
     }
     // (a) release: everything before this call (earlier launches' resets
     // included, through stream order) is ordered before this call's pushes
-    fence_acq_rel_sys();
+    ar_fence<1>();
     // owners q with a row at index b: q*per+b < rows
     const int nq = min(world, (rows - 1 - b) / per + 1);
     if (role == 0) {
@@ -274,7 +287,7 @@ __global__ void __launch_bounds__(1024)
           // that needs its rows times out as well instead of reading garbage.
           if (!dead) {
             // (b) acquire the receive polls, release before the gather pushes
-            fence_acq_rel_sys();
+            ar_fence<2>();
 #pragma unroll
             for (int p = 0; p < MAXW; ++p) {
               if (p < world) {
@@ -332,7 +345,7 @@ __global__ void __launch_bounds__(1024)
     }
     // (c) acquire the gather polls: what a peer did before its gather push is
     // ordered before this rank's next pushes
-    fence_acq_rel_sys();
+    ar_fence<4>();
     if (__syncthreads_or(dead)) {
       if (threadIdx.x == 0) {
         set_error(kErrTimeout);

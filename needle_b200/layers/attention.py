@@ -28,6 +28,15 @@ from .. import ops
 from .linear import ColumnParallelLinear, RowParallelLinear
 
 
+def _aligned16(*ts) -> bool:
+    """Every tensor starts on a 16-byte boundary and its rows stay on one (the
+    slot writers move 16-byte vectors)."""
+    for t in ts:
+        if t.data_ptr() % 16 or (t.stride(0) * t.element_size()) % 16:
+            return False
+    return True
+
+
 class Attention(nn.Module):
     def __init__(self, config, layer_idx: int, tp_size: int = 1, tp_rank: int = 0,
                  qkv_bias: bool = False):
@@ -70,7 +79,10 @@ class Attention(nn.Module):
                 o += n
 
     def forward(self, hidden_states, positions, kv_cache, block_table, cu_seqlens,
-                context_lens, max_seqlen, is_prefill, cos, sin):
+                context_lens, max_seqlen, is_prefill, cos, sin, slot_mapping=None):
+        """needle's ``Attention.forward``; ``slot_mapping`` (optional, not in
+        needle's signature) is the forward's KV slot table from
+        ``ops.slot_mapping``, built once and shared by all layers."""
         T = hidden_states.shape[0]
         H, KV, D = self.num_heads, self.num_kv_heads, self.head_dim
         # getattr: patch_needle() binds this method to needle's own Attention,
@@ -86,12 +98,17 @@ class Attention(nn.Module):
             q = self.q_proj(hidden_states).view(T, H, D)
             k = self.k_proj(hidden_states).view(T, KV, D)
             v = self.v_proj(hidden_states).view(T, KV, D)
-        if is_prefill:
+        if slot_mapping is not None and _aligned16(q, k, v, cos, sin):
+            ops.rope_store_kvcache_slots(q, k, v, cos, sin, kv_cache, slot_mapping,
+                                         write_k_back=is_prefill)
+        elif is_prefill:
             ops.rope_store_kvcache(q, k, v, cos, sin, kv_cache, block_table, context_lens,
                                    cu_seqlens=cu_seqlens, write_k_back=True)
-            attn = ops.prefill_attention(q, k, v, cu_seqlens, max_seqlen, self.scale)
         else:
             ops.rope_store_kvcache(q, k, v, cos, sin, kv_cache, block_table, context_lens)
+        if is_prefill:
+            attn = ops.prefill_attention(q, k, v, cu_seqlens, max_seqlen, self.scale)
+        else:
             plan = ops.decode_plan(T, H, KV, D, block_table.shape[1], kv_cache.shape[3],
                                    q.device)
             attn = ops.paged_decode(q, kv_cache, block_table, context_lens, self.scale,

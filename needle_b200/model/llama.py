@@ -61,16 +61,18 @@ class LlamaDecoderLayer(nn.Module):
         self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
 
     def forward(self, hidden_states, residual, positions, kv_cache, block_table, cu_seqlens,
-                context_lens, max_seqlen, is_prefill, cos, sin):
+                context_lens, max_seqlen, is_prefill, cos, sin, slot_mapping=None):
         """``residual`` is None for the first layer; otherwise ``hidden_states``
-        is the previous layer's MLP output still to be added to it."""
+        is the previous layer's MLP output still to be added to it.
+        ``slot_mapping``: the forward's KV slot table (built once for all
+        layers), or None."""
         if residual is None:
             residual = hidden_states
             x = self.input_layernorm(hidden_states)
         else:
             x, residual = self.input_layernorm(hidden_states, residual)
         x = self.self_attn(x, positions, kv_cache, block_table, cu_seqlens, context_lens,
-                           max_seqlen, is_prefill, cos, sin)
+                           max_seqlen, is_prefill, cos, sin, slot_mapping=slot_mapping)
         x, residual = self.post_attention_layernorm(x, residual)
         return self.mlp(x), residual
 
@@ -91,10 +93,18 @@ class LlamaModel(nn.Module):
                 max_seqlen, is_prefill):
         cos, sin = self.rotary_emb.get_cos_sin(positions)
         h = self.embed_tokens(input_ids)
+        # every layer writes its new K/V rows to the same cache slots: resolve
+        # them once (needle recomputes them per layer, attention.py:140-154,
+        # 204-246)
+        c0 = kv_caches[0]
+        slots = ops.slot_mapping(block_table, context_lens, c0.shape[1], c0.shape[3],
+                                 cu_seqlens=cu_seqlens if is_prefill else None,
+                                 num_tokens=input_ids.shape[0])
         residual = None
         for i, layer in enumerate(self.layers):
             h, residual = layer(h, residual, positions, kv_caches[i], block_table, cu_seqlens,
-                                context_lens, max_seqlen, is_prefill, cos, sin)
+                                context_lens, max_seqlen, is_prefill, cos, sin,
+                                slot_mapping=slots)
         h, _ = self.norm(h, residual)
         return h
 

@@ -46,6 +46,16 @@ def build_model(config: ModelConfig, tp_size: int = 1, tp_rank: int = 0):
     raise ValueError(f"Unsupported model_type: {mt!r}")
 
 
+def _part(sched_out, prefill: bool):
+    """The prefill (or decode) half of a mixed ``SchedulerOutput``, as needle
+    builds it for its two forwards (``needle/model/runner.py:121-142``)."""
+    return SchedulerOutput(
+        prefill_seqs=list(sched_out.prefill_seqs) if prefill else [],
+        decode_seqs=[] if prefill else list(sched_out.decode_seqs),
+        block_tables=sched_out.block_tables, swap_in_map={}, swap_out_map={},
+        blocks_to_free=[])
+
+
 class _InputStage:
     """Pinned staging for a step's host-built input arrays.
 
@@ -68,6 +78,7 @@ class _InputStage:
         self.events = [torch.cuda.Event() for _ in range(slots)]
         self.recorded = [False] * slots
         self.next = 0
+        self.bytes_copied = 0  # host-to-device bytes moved so far (one copy per put)
 
     def put(self, arrays: List[np.ndarray], table=None) -> List[torch.Tensor]:
         """Device views of ``arrays`` and, if ``table = (rows, width, pad)``
@@ -103,6 +114,7 @@ class _InputStage:
         db = self.dev[k]
         if total:
             db[:total].copy_(self.host[k][:total], non_blocking=True)
+            self.bytes_copied += total
         self.events[k].record(torch.cuda.current_stream(self.device))
         self.recorded[k] = True
         out = [db[o:o + a.nbytes].view(self._TORCH[a.dtype]).view(a.shape)
@@ -265,13 +277,12 @@ class ModelRunner:
         all_seqs = list(sched_out.prefill_seqs) + list(sched_out.decode_seqs)
         with torch.no_grad():
             if sched_out.prefill_seqs and sched_out.decode_seqs:
-                pre = self._prepare_inputs(sched_out.prefill_seqs, [], sched_out.block_tables)
-                dec = self._prepare_inputs([], sched_out.decode_seqs, sched_out.block_tables)
+                # mixed batch: two forwards, as needle (runner.py:121-148)
+                pre = self._prepare_inputs(_part(sched_out, prefill=True))
+                dec = self._prepare_inputs(_part(sched_out, prefill=False))
                 logits = torch.cat([self._forward(pre), self._forward(dec)], dim=0)
             else:
-                inp = self._prepare_inputs(sched_out.prefill_seqs, sched_out.decode_seqs,
-                                           sched_out.block_tables)
-                logits = self._forward(inp)
+                logits = self._forward(self._prepare_inputs(sched_out))
         params = [s.request.sampling_params for s in all_seqs]
         ids = self.sampler.sample(logits, params)   # synchronises with the step's kernels
         if self.tp_comm is not None:
@@ -401,12 +412,16 @@ class ModelRunner:
             self._stage = _InputStage(self.device)
         return self._stage.put(arrays, table)
 
-    def _prepare_inputs(self, prefill_seqs, decode_seqs, block_tables) -> ExecuteInput:
-        """Same tensors as ``needle/model/runner.py:194-249``: a sequence with
-        nothing generated feeds its whole prompt at context 0, any other feeds
-        its last token at context ``length - 1``; block-table rows are padded
+    def _prepare_inputs(self, sched_out) -> ExecuteInput:
+        """``needle/model/runner.py:194-249`` with needle's signature: the same
+        tensors from a ``SchedulerOutput`` (its ``prefill_seqs``,
+        ``decode_seqs`` and ``block_tables``).  A sequence with nothing
+        generated feeds its whole prompt at context 0, any other feeds its
+        last token at context ``length - 1``; block-table rows are padded
         (here with the reserved padding block).  Built with numpy; pure decode
         batches take a vectorised path."""
+        prefill_seqs, decode_seqs = sched_out.prefill_seqs, sched_out.decode_seqs
+        block_tables = sched_out.block_tables
         all_seqs = list(prefill_seqs) + list(decode_seqs)
         is_prefill = len(decode_seqs) == 0 or len(prefill_seqs) > 0
         B = len(all_seqs)

@@ -109,6 +109,69 @@ def store_kvcache(k: torch.Tensor, v: torch.Tensor, kv_cache: torch.Tensor,
         context_lens.data_ptr(), context_lens.shape[0], k.shape[0], dt, _stream(k)))
 
 
+def slot_mapping(block_table: torch.Tensor, context_lens: torch.Tensor, num_blocks: int,
+                 block_size: int, cu_seqlens: Optional[torch.Tensor] = None,
+                 num_tokens: Optional[int] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The forward's slot table ``[T]`` int32 (``block * block_size + offset``
+    of every new token, -1 = not written), built once and read by every
+    layer's ``store_kvcache_slots`` / ``rope_store_kvcache_slots``.
+    ``cu_seqlens=None`` is the decode case (one token per sequence)."""
+    _cuda(block_table, context_lens, cu_seqlens, out)
+    bts, maxb = _bt(block_table)
+    _i32(context_lens, "context_lens")
+    B = context_lens.shape[0]
+    if cu_seqlens is not None:
+        _i32(cu_seqlens, "cu_seqlens")
+        if num_tokens is None:
+            raise ValueError("num_tokens is required with cu_seqlens (no device read)")
+    T = B if cu_seqlens is None else int(num_tokens)
+    if out is None:
+        out = torch.empty(T, dtype=torch.int32, device=context_lens.device)
+    elif out.dtype != torch.int32 or out.numel() < T or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int32 tensor of at least T elements")
+    L.check(L.lib().nb_slot_mapping(
+        block_table.data_ptr(), bts, maxb,
+        cu_seqlens.data_ptr() if cu_seqlens is not None else None, context_lens.data_ptr(), B,
+        T, block_size, num_blocks, out.data_ptr(), _stream(context_lens)))
+    return out[:T]
+
+
+def store_kvcache_slots(k: torch.Tensor, v: torch.Tensor, kv_cache: torch.Tensor,
+                        slots: torch.Tensor) -> None:
+    """``store_kvcache`` with positions from a slot table (``slot_mapping``)."""
+    _cuda(k, v, kv_cache, slots)
+    n, kvh, bs, d = _cache_dims(kv_cache)
+    _i32(slots, "slots")
+    if k.dtype != kv_cache.dtype or v.dtype != kv_cache.dtype:
+        raise TypeError("k/v dtype must match the cache")
+    if slots.shape[0] < k.shape[0]:
+        raise ValueError("fewer slots than tokens")
+    L.check(L.lib().nb_store_kvcache_slots(
+        k.data_ptr(), _rows(k, "k"), v.data_ptr(), _rows(v, "v"), kv_cache.data_ptr(),
+        n, kvh, bs, d, slots.data_ptr(), k.shape[0], _dtype(kv_cache), _stream(k)))
+
+
+def rope_store_kvcache_slots(q, k, v, cos, sin, kv_cache, slots,
+                             write_k_back: bool = False) -> None:
+    """``rope_store_kvcache`` with positions from a slot table."""
+    _cuda(q, k, v, cos, sin, kv_cache, slots)
+    n, kvh, bs, d = _cache_dims(kv_cache)
+    _i32(slots, "slots")
+    for t in (q, k, v, cos, sin):
+        if t.dtype != kv_cache.dtype:
+            raise TypeError("q/k/v/cos/sin dtype must match the cache")
+    if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
+        raise ValueError("cos/sin must share a row stride with unit column stride")
+    if slots.shape[0] < q.shape[0]:
+        raise ValueError("fewer slots than tokens")
+    L.check(L.lib().nb_rope_store_kvcache_slots(
+        q.data_ptr(), _rows(q, "q"), q.shape[1], k.data_ptr(), _rows(k, "k"),
+        v.data_ptr(), _rows(v, "v"), cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+        kv_cache.data_ptr(), n, kvh, bs, d, slots.data_ptr(), q.shape[0],
+        int(bool(write_k_back)), _dtype(kv_cache), _stream(q)))
+
+
 def rope_(q: torch.Tensor, k: Optional[torch.Tensor], cos: torch.Tensor,
           sin: torch.Tensor) -> None:
     """In-place NeoX RoPE of ``q [T, Hq, D]`` and ``k [T, Hkv, D]``."""

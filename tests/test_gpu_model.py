@@ -177,7 +177,10 @@ def test_runner_bf16_first_token_logits_vs_oracle(cuda):
                      token_ids=list(p), logical_blocks=[], block_size=16)
             for i, p in enumerate(prompts)]
     tables = {1: [0, 1], 2: [2, 3, 4, 5], 3: [6]}
-    inp = runner._prepare_inputs(seqs, [], tables)
+    from needle_b200.model.sequence import SchedulerOutput
+    inp = runner._prepare_inputs(SchedulerOutput(prefill_seqs=seqs, decode_seqs=[],
+                                                 block_tables=tables, swap_in_map={},
+                                                 swap_out_map={}, blocks_to_free=[]))
     with torch.no_grad():
         logits = runner._forward(inp).float().cpu()
     from oracle.model_oracle import prepare_inputs

@@ -13,7 +13,8 @@ import torch
 
 from needle_b200.model import steppack
 from needle_b200.model.runner import ModelRunner
-from needle_b200.model.sequence import Request, SamplingParams, Sequence, SequenceStatus
+from needle_b200.model.sequence import (Request, SamplingParams, SchedulerOutput, Sequence,
+                                         SequenceStatus)
 from oracle import model_oracle as mo
 
 
@@ -41,7 +42,9 @@ def _seq(sid, tokens, generated):
 
 def _check(prefill, decode, tables):
     r = _HostRunner()
-    got = r._prepare_inputs(prefill, decode, tables)
+    got = r._prepare_inputs(SchedulerOutput(prefill_seqs=list(prefill), decode_seqs=list(decode),
+                                            block_tables=tables, swap_in_map={},
+                                            swap_out_map={}, blocks_to_free=[]))
     seqs = [dict(id=s.seq_id, tokens=s.token_ids, generated=s.num_generated_tokens)
             for s in list(prefill) + list(decode)]
     ref = mo.prepare_inputs(seqs, tables, num_gpu_blocks=1000)
