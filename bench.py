@@ -68,7 +68,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload",
                     choices=["llama8b", "llama8b-c4", "qwen72b", "decode-op", "prefill",
-                             "allreduce", "store-kv"],
+                             "allreduce", "store-kv", "kernel-cases"],
                     default="llama8b",
                     help="llama8b (default): config 3, Llama-3-8B decode at batch 256, tp=N; "
                          "llama8b-c4: config 4 (512 requests, tp=N); qwen72b: config 5 (tp=N, "
@@ -1105,6 +1105,111 @@ def run_store_kv(args):
         dist.destroy_process_group()
 
 
+def run_kernel_cases(args):
+    """Per-kernel roofline figures for the kernels around the decode and
+    prefill paths, each call timed alone with CUDA events on the launching
+    stream after an L2 flush (a 256 MB write), averaged over ``--steps``
+    calls: achieved = algorithmic bytes (or FLOPs) / time.  One JSON line."""
+    rank, local, ws = dist_init(args.gpus)
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    from needle_b200 import ops
+    from needle_b200.synth import decode_op_workload
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(0)
+    rnd = lambda *shape: torch.randn(*shape, device=dev, generator=g, dtype=bf)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+    peak, src = measured_hbm_peak()
+    iters = max(5, min(args.steps, 100))
+    res = {}
+
+    def case(name, kernels, nbytes, fn, bound="hbm", flops=None):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        tot = 0.0
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize(dev)
+            tot += e0.elapsed_time(e1)
+        ms = tot / iters
+        r = {"kernels": kernels, "ms": round(ms, 5), "alg_bytes": int(nbytes),
+             "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1)}
+        if bound == "hbm":
+            r["frac"] = round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)
+        if flops:
+            r["TFLOP/s"] = round(flops / (ms * 1e-3) / 1e12, 1)
+        r["bound"] = bound
+        res[name] = r
+
+    H = 4096
+    for T, tag in ((256, "decode 256"), (8192, "prefill 8192")):
+        x, r, w = rnd(T, H), rnd(T, H), rnd(H)
+        o, ro = torch.empty_like(x), torch.empty_like(x)
+        case(f"fused_add_rmsnorm {tag} x 4096", "rmsnorm_kernel<ADD>", 4 * T * H * 2 + H * 2,
+             lambda: ops.fused_add_rmsnorm(x, r, w, 1e-5, out=o, residual_out=ro))
+    x, w = rnd(8192, H), rnd(H)
+    o = torch.empty_like(x)
+    case("rmsnorm prefill 8192 x 4096", "rmsnorm_kernel", 2 * 8192 * H * 2 + H * 2,
+         lambda: ops.rmsnorm(x, w, 1e-5, out=o))
+    inter = 14336
+    for T, tag in ((256, "decode 256"), (8192, "prefill 8192")):
+        gu = rnd(T, 2 * inter)
+        o = torch.empty(T, inter, dtype=bf, device=dev)
+        case(f"silu_mul {tag} x 14336", "silu_mul_kernel", 3 * T * inter * 2,
+             lambda: ops.silu_mul(gu, out=o))
+    del x, r, w, o, ro, gu
+    # paged decode: config 2 (tensor-core split + merge) and the SIMT kernel
+    # at GQA group 16 (32 query / 2 KV heads)
+    for kvh, tag, kern in ((8, "config 2 (group 4)", "paged_decode_tc_kernel + decode_merge_kernel"),
+                           (2, "group 16 (32/2 heads)", "paged_decode_simt_kernel + decode_merge_kernel")):
+        wl = decode_op_workload(batch=64, num_heads=32, num_kv_heads=kvh, head_dim=128,
+                                block_size=16, device=dev)
+        B, maxb = wl["block_table"].shape
+        plan = ops.DecodePlan(B, 32, kvh, 128, maxb, 16, dev)
+        out = torch.empty_like(wl["q"])
+        case(f"paged_decode {tag}", kern, decode_alg_bytes(wl["seq_len"], kvh, 32, 128, 2),
+             lambda: ops.paged_decode(wl["q"], wl["kv_cache"], wl["block_table"],
+                                      wl["context_lens"], wl["scale"], out=out, plan=plan))
+        del wl, plan, out
+        torch.cuda.empty_cache()
+    # the prefill-size slot table
+    Bp, S, N = 8, 1024, 20000
+    perm = torch.randperm(N, generator=torch.Generator().manual_seed(0))[:Bp * S // 16]
+    bt = perm.view(Bp, S // 16).to(device=dev, dtype=torch.int32)
+    ctx = torch.zeros(Bp, dtype=torch.int32, device=dev)
+    cu = torch.arange(0, Bp * S + 1, S, dtype=torch.int32, device=dev)
+    slots = torch.empty(Bp * S, dtype=torch.int32, device=dev)
+    case("slot_mapping prefill 8 x 1024", "slot_mapping_prefill_kernel",
+         Bp * S * 4 + bt.numel() * 4 + 2 * Bp * 4,
+         lambda: ops.slot_mapping(bt, ctx, N, 16, cu_seqlens=cu, num_tokens=Bp * S, out=slots))
+    # KV block swap: 32 layers x 64 blocks, device -> pinned host and back
+    L_, nb, kv, D = 32, 256, 8, 128
+    gpu = [rnd(2, nb, kv, 16, D) for _ in range(L_)]
+    cpu = [torch.empty(2, nb, kv, 16, D, dtype=bf).pin_memory() for _ in range(L_)]
+    pairs = torch.stack([torch.arange(0, 128, 2), torch.arange(64)], 1).to(torch.int32).to(dev)
+    nbytes = L_ * 64 * 2 * kv * 16 * D * 2
+    case("swap_kv_blocks gpu->pinned 32 layers x 64 blocks", "swap_blocks_kernel", nbytes,
+         lambda: ops.swap_kv_blocks(gpu, cpu, pairs), bound="host link")
+    del gpu, cpu
+    torch.cuda.empty_cache()
+    errs = ops.device_errors()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "per-kernel achieved bandwidth (kernel cases)", "value": None,
+            "unit": "GB/s", "n_gpus": ws, "steps": iters, "warmup": 3, "ms_per_step": None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, N(0,1))",
+            "config": {"workload": "kernel-cases: each call alone after a 256 MB L2 flush"},
+            "peak": peak, "peak_source": src, "cases": res, "device_errors": errs,
+            "gpu_launches": None}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1115,6 +1220,8 @@ def main():
         run_allreduce(args)
     elif args.workload == "store-kv":
         run_store_kv(args)
+    elif args.workload == "kernel-cases":
+        run_kernel_cases(args)
     elif args.workload in MODEL_WORKLOADS:
         run_model(args)
     else:

@@ -646,8 +646,10 @@ int launch_prefill_tc2(const void* q, int64_t qs, const void* k, int64_t ks, con
 
 inline int prefill_version() {
   static int v = [] {
-    const char* e = getenv("NB_PREFILL_V");  // "1": single-group kernel (diagnostics)
-    return (e && e[0] == '1') ? 1 : 2;
+    // "1": single-group kernel, "3": the persistent kernel (prefill3.cuh);
+    // default: the per-unit two-group kernel
+    const char* e = getenv("NB_PREFILL_V");
+    return (e && e[0] == '1') ? 1 : (e && e[0] == '3') ? 3 : 2;
   }();
   return v;
 }
@@ -675,6 +677,8 @@ int launch_prefill_simt_d(int D, const void* q, int64_t qs, const void* k, int64
 }
 
 }  // namespace nbh
+
+#include "prefill3.cuh"
 
 extern "C" {
 
@@ -706,6 +710,13 @@ int nb_prefill_attention(const void* q, int64_t q_stride, const void* k, int64_t
   if (tc) {
 #define NB_ARGS q, q_stride, k, k_stride, v, v_stride, num_q_heads, num_kv_heads, group,         \
                 cu_seqlens, num_seqs, num_tokens, max_seqlen, sl2, out, out_stride, dtype, st
+    if (prefill_version() == 3) {
+      if (dtype == NB_DTYPE_BF16)
+        return head_dim == 64 ? launch_prefill_tc3<__nv_bfloat16, 64>(NB_ARGS)
+                              : launch_prefill_tc3<__nv_bfloat16, 128>(NB_ARGS);
+      return head_dim == 64 ? launch_prefill_tc3<__half, 64>(NB_ARGS)
+                            : launch_prefill_tc3<__half, 128>(NB_ARGS);
+    }
     if (prefill_version() == 2) {
       if (dtype == NB_DTYPE_BF16)
         return head_dim == 64 ? launch_prefill_tc2<__nv_bfloat16, 64>(NB_ARGS)

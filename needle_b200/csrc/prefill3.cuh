@@ -1,0 +1,477 @@
+// Persistent, warp-specialised causal prefill on tcgen05 + TMEM.
+//
+// Same mathematics, operand layouts and MMA descriptors as prefill_tc2_kernel
+// (two 128-row query tiles A and B of one (head, sequence) share every K/V
+// tile; S = Q K^T and O += P V on the tensor cores with fp32 accumulators in
+// tensor memory; P written back over S as bf16/fp16 and read by the P.V MMA
+// straight from tensor memory; the running max raised lazily), scheduled
+// differently:
+//
+//   * Persistent grid: one CTA per SM walks work units (256 query rows, query
+//     head, sequence) in a static order that puts the units with the most KV
+//     tiles first (the last query blocks of the longest sequences), so the
+//     causal triangle's long units start early and short ones fill the tail.
+//     Tensor memory is allocated once per CTA, not once per unit.
+//   * Ten warps: warp 0 issues TMA loads, warp 1 issues the MMAs (one lane),
+//     warps 2-5 and 6-9 run the softmax of tiles A and B (thread = query row
+//     = TMEM lane) and the epilogue.  K and V have separate two-stage rings
+//     with their own "free" barriers: K_j is released as soon as both S MMAs
+//     that read it finish, V_j after both P.V MMAs.
+//   * A softmax thread loads its 128 scores from tensor memory with four
+//     loads and one wait, keeps them in registers for the max and the
+//     exponentials, and stores P back with four stores and one wait.
+//   * The next unit's Q tiles load as soon as the current unit's last S MMA
+//     has finished, and its first S MMAs run while the softmax warps write
+//     out the current unit's O (tensor memory O is handed back to the MMA warp
+//     through an "O free" barrier after the epilogue read it).
+//
+// Every wait is bounded (kWaitLimitNs).  A role that gives up sets an abort
+// flag in shared memory and records NB_DEVERR_TIMEOUT; every role checks the
+// flag between steps and leaves the unit loop; before the CTA exits the
+// producer waits (bounded) for its copies in flight and the MMA warp for its
+// MMAs, then tensor memory is freed.
+#pragma once
+#include "nb_common.cuh"
+
+namespace nb {
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane, without waiting
+// (pair with tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+// Store 8 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int D> struct Pf3Geom {
+  static constexpr int kAtom = 128 * 128;       // 128 rows x 128 B
+  static constexpr int kTile = (D / 64) * kAtom;
+  static constexpr int kQA = 0;
+  static constexpr int kQB = kTile;
+  static constexpr int kK = 2 * kTile;          // K ring: 2 stages
+  static constexpr int kV = kK + 2 * kTile;     // V ring: 2 stages
+  static constexpr int kBars = kV + 2 * kTile;
+  static constexpr int kSmem = kBars + 256 + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kSA = 0, kSB = 128, kOA = 256, kOB = 256 + D;
+  static constexpr int kThreads = 320;
+};
+
+// Work unit u -> (query block, head, sequence); units with the most KV tiles
+// come first.  Units past a sequence's end are empty (every role skips them).
+struct Pf3Unit {
+  int qb, h, b;
+};
+__device__ __forceinline__ Pf3Unit pf3_unit(int u, int hq, int B, int nqb) {
+  const int per = hq * B;
+  const int r = u % per;
+  return Pf3Unit{nqb - 1 - u / per, r % hq, r / hq};
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(320, 1)
+    prefill_tc3_kernel(const __grid_constant__ CUtensorMap qmap,
+                       const __grid_constant__ CUtensorMap kmap,
+                       const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
+                       int B, int hq, int group, int nqb, float scale_log2, T* __restrict__ out,
+                       int64_t os) {
+  using G = Pf3Geom<D>;
+  constexpr bool kBf16 = !__is_same(T, __half);
+  constexpr uint32_t kIdS = idesc_f16_f32(kBf16, 128, 128, false, false);
+  constexpr uint32_t kIdO = idesc_f16_f32(kBf16, 128, D, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sb = smem_u32(smem);
+  // barriers (8 bytes each)
+  const uint32_t bar_q = sb + G::kBars;            // Q_A (+Q_B) landed
+  const uint32_t bar_k = bar_q + 8;                // [2] K stage landed
+  const uint32_t bar_v = bar_q + 24;               // [2] V stage landed
+  const uint32_t bar_kfree = bar_q + 40;           // [2] K stage read by its S MMAs
+  const uint32_t bar_vfree = bar_q + 56;           // [2] V stage read by its P.V MMAs
+  const uint32_t bar_qfree = bar_q + 72;           // this unit's S MMAs done: Q may reload
+  const uint32_t bar_s = bar_q + 80;               // [2] S_A / S_B ready
+  const uint32_t bar_p = bar_q + 96;               // [2] P_A / P_B written (128 arrivals)
+  const uint32_t bar_o = bar_q + 112;              // [2] O_A / O_B final
+  const uint32_t bar_ofree = bar_q + 128;          // [2] O_A / O_B read out (128 arrivals)
+  const uint32_t bar_end = bar_q + 144;            // every MMA of the CTA finished
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G::kBars + 192);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kBars + 200);
+
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), G::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    mbar_init(bar_q, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_k + 8 * i, 1);
+      mbar_init(bar_v + 8 * i, 1);
+      mbar_init(bar_kfree + 8 * i, 1);
+      mbar_init(bar_vfree + 8 * i, 1);
+      mbar_init(bar_s + 8 * i, 1);
+      mbar_init(bar_p + 8 * i, 128);
+      mbar_init(bar_o + 8 * i, 1);
+      mbar_init(bar_ofree + 8 * i, 128);
+    }
+    mbar_init(bar_qfree, 1);
+    mbar_init(bar_end, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_units = nqb * hq * B;
+
+  // Causal extent of a unit: KV tiles under tile A / tile B (0: no tile B).
+  auto extent = [&](const Pf3Unit& w, int& s0, int& len, int& nA, int& nB) -> bool {
+    s0 = __ldg(cu + w.b);
+    len = __ldg(cu + w.b + 1) - s0;
+    const int q0 = w.qb * 256;
+    if (q0 >= len) return false;
+    nA = 2 * w.qb + 1;
+    nB = q0 + 128 < len ? 2 * w.qb + 2 : 0;
+    return true;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t nq = 0, nk = 0, nv = 0;  // loads issued (running counts)
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        const Pf3Unit w = pf3_unit(u, hq, B, nqb);
+        int s0, len, nA, nB;
+        if (!extent(w, s0, len, nA, nB)) continue;
+        const int kh = w.h / group, q0 = w.qb * 256;
+        const int n_kv = nB ? nB : nA;
+        if (nq > 0 && !mbar_wait_bounded(bar_qfree, (nq - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(bar_q, (nB ? 2 : 1) * G::kTile);
+#pragma unroll
+        for (int a = 0; a < D / 64; ++a) {
+          tma_load_2d(sb + G::kQA + a * G::kAtom, &qmap, w.h * D + a * 64, s0 + q0, bar_q);
+          if (nB)
+            tma_load_2d(sb + G::kQB + a * G::kAtom, &qmap, w.h * D + a * 64, s0 + q0 + 128,
+                        bar_q);
+        }
+        ++nq;
+        for (int j = 0; j < n_kv; ++j) {
+          if (*abort_flag) { ok = false; break; }
+          const uint32_t st = nk & 1;
+          if (nk >= 2 && !mbar_wait_bounded(bar_kfree + 8 * st, ((nk >> 1) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_k + 8 * st, G::kTile);
+#pragma unroll
+          for (int a = 0; a < D / 64; ++a)
+            tma_load_2d(sb + G::kK + st * G::kTile + a * G::kAtom, &kmap, kh * D + a * 64,
+                        s0 + j * 128, bar_k + 8 * st);
+          ++nk;
+          if (nv >= 2 && !mbar_wait_bounded(bar_vfree + 8 * st, ((nv >> 1) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_v + 8 * st, G::kTile);
+#pragma unroll
+          for (int a = 0; a < D / 64; ++a)
+            tma_load_2d(sb + G::kV + st * G::kTile + a * G::kAtom, &vmap, kh * D + a * 64,
+                        s0 + j * 128, bar_v + 8 * st);
+          ++nv;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        set_error(kErrTimeout);
+      }
+      // copies still in flight land before the CTA may exit: wait (bounded)
+      // for the last phase of every barrier a load was issued on
+      if (nq) mbar_wait_bounded(bar_q, (nq - 1) & 1);
+      for (uint32_t i = (nk > 2 ? nk - 2 : 0); i < nk; ++i)
+        mbar_wait_bounded(bar_k + 8 * (i & 1), (i >> 1) & 1);
+      for (uint32_t i = (nv > 2 ? nv - 2 : 0); i < nv; ++i)
+        mbar_wait_bounded(bar_v + 8 * (i & 1), (i >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t nq = 0, nk = 0, nv = 0;           // tiles consumed (running counts)
+      uint32_t np[2] = {0, 0}, no[2] = {0, 0};   // P tiles consumed, units finished per group
+      bool ok = true;
+      auto wait = [&](uint32_t bar, uint32_t par) {
+        if (!ok) return false;
+        if (*abort_flag || !mbar_wait_bounded(bar, par)) ok = false;
+        return ok;
+      };
+      auto issue_s = [&](uint32_t q_off, uint32_t kst, uint32_t t_col) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
+          tc_mma_f16_ss(tmem + t_col, smem_desc_sw128(sb + q_off + off, 16, 1024),
+                        smem_desc_sw128(kst + off, 16, 1024), kIdS, kk > 0);
+        }
+      };
+      auto issue_pv = [&](uint32_t vst, uint32_t s_col, uint32_t o_col, bool first) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16_ts(tmem + o_col, tmem + s_col + kk * 8,
+                        smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
+                        (!first || kk > 0) ? 1u : 0u);
+      };
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        const Pf3Unit w = pf3_unit(u, hq, B, nqb);
+        int s0, len, nA, nB;
+        if (!extent(w, s0, len, nA, nB)) continue;
+        const int n_kv = nB ? nB : nA;
+        const int nx[2] = {nA, nB};
+        const uint32_t qoff[2] = {(uint32_t)G::kQA, (uint32_t)G::kQB};
+        const uint32_t scol[2] = {G::kSA, G::kSB}, ocol[2] = {G::kOA, G::kOB};
+        if (!wait(bar_q, nq & 1)) break;
+        ++nq;
+        // S_X(0) for both tiles
+        {
+          const uint32_t st = nk & 1;
+          if (!wait(bar_k + 8 * st, (nk >> 1) & 1)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (!nx[x]) continue;
+            issue_s(qoff[x], sb + G::kK + st * G::kTile, scol[x]);
+            tc_commit(bar_s + 8 * x);
+          }
+          tc_commit(bar_kfree + 8 * st);
+          if (n_kv == 1) tc_commit(bar_qfree);
+          ++nk;
+        }
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const uint32_t vst = nv & 1;
+          if (!wait(bar_v + 8 * vst, (nv >> 1) & 1)) break;
+          const bool has_next = j + 1 < n_kv;
+          const uint32_t kst = nk & 1;
+          bool k_ready = false;
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (!ok) break;
+            if (j >= nx[x]) continue;
+            // P_X(j) written by the softmax group; O_X free on its first tile
+            if (j == 0 && no[x] > 0 && !wait(bar_ofree + 8 * x, (no[x] - 1) & 1)) break;
+            if (!wait(bar_p + 8 * x, np[x] & 1)) break;
+            ++np[x];
+            tc_fence_after();
+            issue_pv(sb + G::kV + vst * G::kTile, scol[x], ocol[x], j == 0);
+            if (j + 1 == nx[x]) {
+              tc_commit(bar_o + 8 * x);  // O_X final for this unit
+              ++no[x];
+            } else {
+              if (!k_ready) {
+                if (!wait(bar_k + 8 * kst, (nk >> 1) & 1)) break;
+                tc_fence_after();
+                k_ready = true;
+              }
+              issue_s(qoff[x], sb + G::kK + kst * G::kTile, scol[x]);
+              tc_commit(bar_s + 8 * x);  // also covers P_X(j).V_j
+            }
+          }
+          if (!ok) break;
+          tc_commit(bar_vfree + 8 * vst);
+          ++nv;
+          if (has_next) {
+            tc_commit(bar_kfree + 8 * kst);
+            if (j + 2 == n_kv) tc_commit(bar_qfree);  // last S MMAs of the unit issued
+            ++nk;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        set_error(kErrTimeout);
+      }
+      tc_commit(bar_end);
+      mbar_wait_bounded(bar_end, 0);  // every MMA issued by this CTA has finished
+    }
+  } else {
+    // ---------------- softmax groups + epilogue ----------------
+    const int x = (warp - 2) >> 2;  // 0 = tile A, 1 = tile B
+    const int wq = (warp - 2) & 3;  // warp quarter = TMEM lanes [32 wq, 32 wq + 32)
+    const uint32_t tS = tmem + (x ? G::kSB : G::kSA);
+    const uint32_t tO = tmem + (x ? G::kOB : G::kOA);
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const int r = wq * 32 + lane;
+    uint32_t ns = 0, nunits = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+      const Pf3Unit w = pf3_unit(u, hq, B, nqb);
+      int s0, len, nA, nB;
+      if (!extent(w, s0, len, nA, nB)) continue;
+      const int n_mine = x ? nB : nA;
+      if (n_mine == 0) continue;
+      const int qi = w.qb * 256 + x * 128 + r;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_mine; ++j) {
+        const bool got = mbar_wait_bounded(bar_s + 8 * x, ns & 1);
+        ++ns;
+        if (__any_sync(0xffffffffu, !got) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32_nowait(tS + lane_off + c * 32, sr[c]);
+        tmem_wait_ld();
+        const int kb = j * 128;
+        // whole tile below the diagonal and inside the sequence: no masking
+        const bool full = kb + 127 <= qi && kb + 128 <= len;
+        float mx = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
+        } else {
+          const int lim = min(qi, len - 1) - kb;  // last visible column of the row
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
+              mx = fmaxf(mx, __uint_as_float(sr[c][i]));
+            }
+        }
+        mx *= scale_log2;  // scale > 0: max of scaled scores = scaled max
+        const bool need = mx > m + kRescaleThreshold;
+        float alpha = 1.f;
+        if (need) {
+          alpha = exp2f(m - mx);
+          m = mx;
+        }
+        const float neg_m = -m;
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              // masked scores are -inf: exp2 gives exactly 0
+              const int i = hh * 16 + 2 * e;
+              const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c][i]), scale_log2, neg_m));
+              const float p1 =
+                  ex2_approx(fmaf(__uint_as_float(sr[c][i + 1]), scale_log2, neg_m));
+              rs += p0 + p1;
+              pk[e] = Mma<T>::pack(p0, p1);
+            }
+            tmem_st8(tS + lane_off + c * 16 + hh * 8, pk);  // P over S's first 64 columns
+          }
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // rescale O_X (P_X(j-1).V_{j-1} is complete: the commit that
+          // signalled S_X(j) covers it; P_X(j).V_j waits for this group's
+          // arrival below)
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            float v[32];
+            tmem_ld32(tO + lane_off + c * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            tmem_st32(tO + lane_off + c * 32, v);
+          }
+        }
+        tmem_wait_st();
+        l = l * alpha + rs;
+        tc_fence_before();
+        mbar_arrive(bar_p + 8 * x);
+      }
+      if (!ok) break;
+      // epilogue: O_X / l -> out rows
+      const bool done = mbar_wait_bounded(bar_o + 8 * x, nunits & 1);
+      if (__any_sync(0xffffffffu, !done) || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv = 1.f / l;
+      T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)w.h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld32(tO + lane_off + c * 32, v);
+        if (qi < len) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pk[e] = Mma<T>::pack(v[k * 8 + 2 * e] * inv, v[k * 8 + 2 * e + 1] * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
+      ++nunits;
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      if (lane == 0) set_error(kErrTimeout);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, G::kTmemCols);
+  }
+}
+
+}  // namespace nb
+
+namespace nbh {
+
+template <typename T, int D>
+int launch_prefill_tc3(const void* q, int64_t qs, const void* k, int64_t ks, const void* v,
+                       int64_t vs, int hq, int hk, int group, const int32_t* cu, int B, int T_,
+                       int max_seqlen, float sl2, void* out, int64_t os, int dtype,
+                       cudaStream_t st) {
+  using G = nb::Pf3Geom<D>;
+  CUtensorMap qm, km, vm;
+  int rc = tensor_map_2d(&qm, q, dtype, (uint64_t)hq * D, T_, (uint64_t)qs * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
+  if (rc) return rc;
+  auto kern = nb::prefill_tc3_kernel<T, D>;
+  if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc3")) return r2;
+  const int nqb = (max_seqlen + 255) / 256;
+  const int64_t units = (int64_t)nqb * hq * B;
+  if (units > INT32_MAX) return fail(NB_ERR_UNSUPPORTED, "too many prefill work units");
+  const int grid = (int)std::min<int64_t>(units, num_sms());
+  kern<<<grid, G::kThreads, G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, sl2, (T*)out, os);
+  return check_launch("prefill_tc3");
+}
+
+}  // namespace nbh

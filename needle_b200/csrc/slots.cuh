@@ -20,25 +20,45 @@
 
 namespace nb {
 
+// Decode form (one token per sequence): one thread per sequence.
 __global__ void __launch_bounds__(256)
-    slot_mapping_kernel(const int32_t* __restrict__ bt, int64_t bt_stride, int maxb,
-                        const int32_t* __restrict__ cu, const int32_t* __restrict__ ctx,
-                        int num_seqs, int num_tokens, int block_size, int num_blocks,
-                        int32_t* __restrict__ slots) {
+    slot_mapping_decode_kernel(const int32_t* __restrict__ bt, int64_t bt_stride, int maxb,
+                               const int32_t* __restrict__ ctx, int num_seqs, int block_size,
+                               int num_blocks, int32_t* __restrict__ slots) {
   griddep_launch_dependents();
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= num_tokens) return;
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= num_seqs) return;
   int phys = -1, off = 0;
-  // token_slot restates needle's index math, clamp and last-token-wins rule
+  // slot_of restates needle's index math, clamp and last-token-wins rule
   const bool ok =
-      token_slot(t, cu, ctx, num_seqs, bt, bt_stride, maxb, num_blocks, block_size, phys, off);
-  slots[t] = ok ? phys * block_size + off : -1;
+      slot_of(s, 0, 1, __ldg(ctx + s), bt, bt_stride, maxb, num_blocks, block_size, phys, off);
+  slots[s] = ok ? phys * block_size + off : -1;
 }
 
-// Cache element offset of (K or V half, slot, KV head h): the head row of the
-// slot's block.  Returns -1 for a slot outside the pool (recorded).
-__device__ __forceinline__ int64_t slot_row(int slot, int which, int h, int num_blocks, int kvh,
-                                            int block_size, int D) {
+// Prefill form: CTAs stride over sequences, a sequence's tokens over threads,
+// so a token costs its sequence's two bounds and one table entry (no search).
+__global__ void __launch_bounds__(256)
+    slot_mapping_prefill_kernel(const int32_t* __restrict__ bt, int64_t bt_stride, int maxb,
+                                const int32_t* __restrict__ cu, const int32_t* __restrict__ ctx,
+                                int num_seqs, int block_size, int num_blocks,
+                                int32_t* __restrict__ slots) {
+  griddep_launch_dependents();
+  for (int s = blockIdx.x; s < num_seqs; s += gridDim.x) {
+    const int c0 = __ldg(cu + s), len = __ldg(cu + s + 1) - c0, c = __ldg(ctx + s);
+    for (int i = threadIdx.x; i < len; i += blockDim.x) {
+      int phys = -1, off = 0;
+      const bool ok =
+          slot_of(s, i, len, c, bt, bt_stride, maxb, num_blocks, block_size, phys, off);
+      slots[c0 + i] = ok ? phys * block_size + off : -1;
+    }
+  }
+}
+
+// Element offset of head 0's row of `slot` in the K half (the V half is
+// `half` elements further; head h is h * block_size * D further).  Returns -1
+// for a slot that is not written or lies outside the pool (recorded).
+__device__ __forceinline__ int64_t slot_base(int slot, int num_blocks, int kvh, int block_size,
+                                             int D) {
   if (slot < 0) return -1;
   const int phys = slot / block_size;
   if (phys >= num_blocks) {
@@ -46,12 +66,13 @@ __device__ __forceinline__ int64_t slot_row(int slot, int which, int h, int num_
     return -1;
   }
   const int off = slot - phys * block_size;
-  return ((((int64_t)which * num_blocks + phys) * kvh + h) * block_size + off) * D;
+  return ((int64_t)phys * kvh * block_size + off) * D;
 }
 
 // K/V rows into the cache.  Unit = (token, U x 32 vectors of the token's
 // kvh x 2 x vpr vectors, ordered (head, K/V, vector)); warps grid-stride over
-// units.  VPR: vectors per head row when known at compile time (0: runtime).
+// units (host-checked to fit int32).  VPR: vectors per head row when known at
+// compile time (0: runtime).
 template <typename T, int VPR, int U>
 __global__ void __launch_bounds__(256)
     store_kvcache_slots_kernel(const T* __restrict__ k, int64_t k_stride, const T* __restrict__ v,
@@ -63,13 +84,14 @@ __global__ void __launch_bounds__(256)
   const int vpr = VPR ? VPR : D / VEC;
   const int per_tok = kvh * 2 * vpr;
   const int upt = (per_tok + 32 * U - 1) / (32 * U);  // units per token
-  const int64_t units = (int64_t)num_tokens * upt;
+  const int units = num_tokens * upt;
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < units;
-       w += nwarps) {
-    const int t = (int)(w / upt);
-    const int j0 = (int)(w - (int64_t)t * upt) * 32 * U;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  const int64_t half = (int64_t)num_blocks * kvh * block_size * D;
+  const int64_t head = (int64_t)block_size * D;
+  for (int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < units; w += nwarps) {
+    const int t = w / upt;
+    const int j0 = (w - t * upt) * 32 * U;
     const int slot = __ldg(slots + t);
     uint4 val[U];
 #pragma unroll
@@ -82,13 +104,16 @@ __global__ void __launch_bounds__(256)
         val[u] = __ldg(reinterpret_cast<const uint4*>(src));
       }
     }
+    const int64_t base = slot_base(slot, num_blocks, kvh, block_size, D);
+    if (base >= 0) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = j0 + u * 32 + lane;
-      if (j < per_tok) {
-        const int vec = j % vpr, r = j / vpr;
-        const int64_t row = slot_row(slot, r & 1, r >> 1, num_blocks, kvh, block_size, D);
-        if (row >= 0) *reinterpret_cast<uint4*>(cache + row + vec * VEC) = val[u];
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + u * 32 + lane;
+        if (j < per_tok) {
+          const int vec = j % vpr, r = j / vpr;
+          T* dst = cache + base + ((r & 1) ? half : 0) + (r >> 1) * head + vec * VEC;
+          *reinterpret_cast<uint4*>(dst) = val[u];
+        }
       }
     }
   }
@@ -112,17 +137,28 @@ __global__ void __launch_bounds__(256)
   const int cpr = CPR ? CPR : half / VEC;
   const int per_tok = (hq + 2 * hk) * cpr;
   const int upt = (per_tok + 32 * U - 1) / (32 * U);
-  const int64_t units = (int64_t)num_tokens * upt;
+  const int units = num_tokens * upt;
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < units;
-       w += nwarps) {
-    const int t = (int)(w / upt);
-    const int j0 = (int)(w - (int64_t)t * upt) * 32 * U;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  const int64_t half_cache = (int64_t)num_blocks * hk * block_size * D;
+  const int64_t head = (int64_t)block_size * D;
+  for (int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < units; w += nwarps) {
+    const int t = w / upt;
+    const int j0 = (w - t * upt) * 32 * U;
     const int slot = __ldg(slots + t);
     const T* cs = cos + (int64_t)t * cs_stride;
     const T* sn = sin + (int64_t)t * cs_stride;
-    T lo[U][VEC], hi[U][VEC];
+    // With cpr dividing 32 a lane's chunk column is the same for every head it
+    // touches, so its cos/sin chunks load once per unit, alongside the rows.
+    constexpr bool kOneCs = CPR != 0 && 32 % (CPR ? CPR : 1) == 0;
+    T lo[U][VEC], hi[U][VEC], cl[VEC], ch[VEC], sl[VEC], sh[VEC];
+    auto load_cs = [&](int c) {
+      *reinterpret_cast<uint4*>(cl) = __ldg(reinterpret_cast<const uint4*>(cs + c));
+      *reinterpret_cast<uint4*>(ch) = __ldg(reinterpret_cast<const uint4*>(cs + c + half));
+      *reinterpret_cast<uint4*>(sl) = __ldg(reinterpret_cast<const uint4*>(sn + c));
+      *reinterpret_cast<uint4*>(sh) = __ldg(reinterpret_cast<const uint4*>(sn + c + half));
+    };
+    if constexpr (kOneCs) load_cs((lane % cpr) * VEC);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * 32 + lane;
@@ -134,17 +170,14 @@ __global__ void __launch_bounds__(256)
       *reinterpret_cast<uint4*>(lo[u]) = *reinterpret_cast<const uint4*>(row + c);
       *reinterpret_cast<uint4*>(hi[u]) = *reinterpret_cast<const uint4*>(row + c + half);
     }
+    const int64_t base = slot_base(slot, num_blocks, hk, block_size, D);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * 32 + lane;
       if (j >= per_tok) continue;
       const int hh = j / cpr, c = (j - hh * cpr) * VEC;
       if (hh < hq + hk) {  // rotate q and k
-        T cl[VEC], ch[VEC], sl[VEC], sh[VEC];
-        *reinterpret_cast<uint4*>(cl) = __ldg(reinterpret_cast<const uint4*>(cs + c));
-        *reinterpret_cast<uint4*>(ch) = __ldg(reinterpret_cast<const uint4*>(cs + c + half));
-        *reinterpret_cast<uint4*>(sl) = __ldg(reinterpret_cast<const uint4*>(sn + c));
-        *reinterpret_cast<uint4*>(sh) = __ldg(reinterpret_cast<const uint4*>(sn + c + half));
+        if constexpr (!kOneCs) load_cs(c);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
           float ol, oh;
@@ -160,14 +193,12 @@ __global__ void __launch_bounds__(256)
           *reinterpret_cast<uint4*>(row + c + half) = *reinterpret_cast<uint4*>(hi[u]);
         }
       }
-      if (hh >= hq) {  // k and v rows into the cache
+      if (hh >= hq && base >= 0) {  // k and v rows into the cache
         const bool is_k = hh < hq + hk;
         const int h = is_k ? hh - hq : hh - hq - hk;
-        const int64_t row = slot_row(slot, is_k ? 0 : 1, h, num_blocks, hk, block_size, D);
-        if (row >= 0) {
-          *reinterpret_cast<uint4*>(cache + row + c) = *reinterpret_cast<uint4*>(lo[u]);
-          *reinterpret_cast<uint4*>(cache + row + c + half) = *reinterpret_cast<uint4*>(hi[u]);
-        }
+        T* dst = cache + base + (is_k ? 0 : half_cache) + h * head + c;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(lo[u]);
+        *reinterpret_cast<uint4*>(dst + half) = *reinterpret_cast<uint4*>(hi[u]);
       }
     }
   }
@@ -198,6 +229,7 @@ int launch_store_slots(const void* k, int64_t ks, const void* v, int64_t vs, voi
   constexpr int U = 4;
   const int per_tok = kvh * 2 * (D / VEC);
   const int64_t units = (int64_t)ntok * ((per_tok + 32 * U - 1) / (32 * U));
+  if (units > INT32_MAX / 2) return fail(NB_ERR_UNSUPPORTED, "too many tokens for one launch");
   const unsigned grid = slot_grid(units);
   if (D / VEC == 16)
     nb::store_kvcache_slots_kernel<T, 16, U><<<grid, 256, 0, st>>>(
@@ -226,6 +258,7 @@ int launch_rope_store_slots(void* q, int64_t qs, int hq, void* k, int64_t ks, co
   const int cpr = D / 2 / VEC;
   const int per_tok = (hq + 2 * hk) * cpr;
   const int64_t units = (int64_t)ntok * ((per_tok + 32 * U - 1) / (32 * U));
+  if (units > INT32_MAX / 2) return fail(NB_ERR_UNSUPPORTED, "too many tokens for one launch");
   const unsigned grid = slot_grid(units);
 #define NB_RSS(C)                                                                              \
   nb::rope_store_slots_kernel<T, C, U><<<grid, 256, 0, st>>>(                                 \
@@ -270,9 +303,15 @@ int nb_slot_mapping(const int32_t* block_table, int64_t block_table_stride,
     return fail(NB_ERR_INVALID_ARG, "cu_seqlens NULL requires num_tokens == num_seqs");
   if (num_tokens == 0) return NB_OK;
   if (num_seqs == 0) return fail(NB_ERR_INVALID_ARG, "tokens without sequences");
-  nb::slot_mapping_kernel<<<(num_tokens + 255) / 256, 256, 0, (cudaStream_t)stream>>>(
-      block_table, block_table_stride, max_blocks_per_seq, cu_seqlens, context_lens, num_seqs,
-      num_tokens, block_size, num_blocks, slots);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!cu_seqlens)
+    nb::slot_mapping_decode_kernel<<<(num_seqs + 255) / 256, 256, 0, st>>>(
+        block_table, block_table_stride, max_blocks_per_seq, context_lens, num_seqs, block_size,
+        num_blocks, slots);
+  else
+    nb::slot_mapping_prefill_kernel<<<std::min(num_seqs, num_sms() * 8), 256, 0, st>>>(
+        block_table, block_table_stride, max_blocks_per_seq, cu_seqlens, context_lens, num_seqs,
+        block_size, num_blocks, slots);
   return check_launch("slot_mapping");
 }
 

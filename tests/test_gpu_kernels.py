@@ -422,11 +422,12 @@ print('ok')
 """
 
 
-@pytest.mark.parametrize("version", ["1", "2"])
+@pytest.mark.parametrize("version", ["1", "2", "3"])
 def test_prefill_every_kernel_version(cuda, version):
-    """Both tensor-core prefill kernels (single softmax group / two ping-pong
-    groups), selected through NB_PREFILL_V in a fresh process, on lengths
-    around the 128- and 256-row tile edges, bf16 and fp16."""
+    """Every tensor-core prefill kernel (single softmax group / two ping-pong
+    groups per CTA / persistent warp-specialised), selected through
+    NB_PREFILL_V in a fresh process, on lengths around the 128- and 256-row
+    tile edges, bf16 and fp16."""
     import os
     import subprocess
     import sys
@@ -435,6 +436,43 @@ def test_prefill_every_kernel_version(cuda, version):
     r = subprocess.run([sys.executable, "-c", _PREFILL_CHECK], cwd=root, env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def _sdpa_fp32(q, k, v, cu, H, kv):
+    """Causal attention per sequence in fp32 with torch on the GPU (GQA by
+    repeating KV heads): the plain reference for large prefill cases."""
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    for s in range(len(cu) - 1):
+        a, b = int(cu[s]), int(cu[s + 1])
+        if b == a:
+            continue
+        qs = q[a:b].float().transpose(0, 1)
+        ks = k[a:b].float().transpose(0, 1).repeat_interleave(H // kv, dim=0)
+        vs = v[a:b].float().transpose(0, 1).repeat_interleave(H // kv, dim=0)
+        out[a:b] = torch.nn.functional.scaled_dot_product_attention(
+            qs, ks, vs, is_causal=True).transpose(0, 1)
+    return out
+
+
+@pytest.mark.parametrize("lens", [[1024] * 16, [3000, 17, 700, 1, 2049, 256, 1500, 90]])
+def test_prefill_many_units_per_cta(cuda, lens):
+    """Batches with many more (query block, head, sequence) units than SMs,
+    so every persistent CTA runs several units back to back (its K/V rings,
+    barrier phases and tensor memory carry over from unit to unit), against
+    fp32 torch attention; bf16, 32/8 heads, D = 128."""
+    ops = _ops()
+    H, kv, D = 32, 8, 128
+    g = torch.Generator(device=cuda).manual_seed(31)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32)
+    T = int(cu[-1])
+    q = torch.randn(T, H, D, device=cuda, generator=g).to(torch.bfloat16)
+    k = torch.randn(T, kv, D, device=cuda, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, kv, D, device=cuda, generator=g).to(torch.bfloat16)
+    out = ops.prefill_attention(q, k, v, cu.to(cuda), max(lens))
+    ref = _sdpa_fp32(q, k, v, cu, H, kv)
+    assert ops.device_errors() == 0
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2, err
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
