@@ -1198,6 +1198,22 @@ def run_kernel_cases(args):
          lambda: ops.swap_kv_blocks(gpu, cpu, pairs), bound="host link")
     del gpu, cpu
     torch.cuda.empty_cache()
+    # the batched sampler at the config 3 decode shape (256 x 128256 bf16):
+    # greedy rows read the row once; sampled rows (top-k 50, top-p 0.9) make
+    # several passes, all but the first from L2
+    n, V = 256, 128256
+    lg = rnd(n, V)
+    ids = torch.empty(n, dtype=torch.int64, device=dev)
+    z = torch.zeros(n, dtype=torch.float32, device=dev)
+    ki = torch.zeros(n, dtype=torch.int32, device=dev)
+    one = torch.ones(n, dtype=torch.float32, device=dev)
+    case("sample greedy 256 x 128256", "sample_kernel", n * V * 2 + n * 8,
+         lambda: ops.sample(lg, z, ki, one, z, out=ids))
+    tt, kk50 = torch.full_like(one, 0.8), torch.full_like(ki, 50)
+    p9, u = torch.full_like(one, 0.9), torch.rand(n, device=dev, generator=g)
+    case("sample top-k 50 / top-p 0.9 256 x 128256", "sample_kernel", n * V * 2 + n * 8,
+         lambda: ops.sample(lg, tt, kk50, p9, u, out=ids))
+    del lg
     errs = ops.device_errors()
     if rank == 0:
         print(json.dumps({

@@ -319,6 +319,29 @@ NB_API int nb_tp_set_wait_limit_ns(uint64_t ns);
 NB_API int nb_silu_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
                        int num_tokens, int intermediate, int dtype, void* stream);
 
+/*
+ * Sampling for a whole decode step in one launch, one row of logits
+ * [num_rows, vocab] (row stride given) per CTA.  Replaces
+ * needle/model/sampler.py:24-46 (a per-row loop with one host read per row).
+ * temperature, top_k, top_p and uniforms are per-row device arrays:
+ *   temperature == 0: greedy, the first index of the maximal logit (NaN
+ *     counts as maximal, as torch.argmax);
+ *   otherwise x = logit / temperature (rounded to the logits' dtype); top_k >
+ *     0 keeps x >= the top_k-th largest x; top_p < 1 then keeps, in
+ *     descending order of x (ties in index order), each token whose
+ *     probability mass before it (softmax over the kept tokens, each
+ *     probability rounded to the logits' dtype, summed in fp32) is at most
+ *     top_p; one token is drawn by inverse CDF in vocabulary order at
+ *     uniforms[row] in [0, 1).
+ * token_ids: [num_rows] int64 (device).  filtered: NULL, or [num_rows, vocab]
+ * of the logits' dtype receiving each sampled row's filtered logits (removed
+ * tokens -inf; greedy rows untouched).
+ */
+NB_API int nb_sample(const void* logits, int64_t row_stride, int num_rows, int vocab,
+                     const float* temperature, const int32_t* top_k, const float* top_p,
+                     const float* uniforms, void* filtered, int64_t filtered_stride,
+                     int64_t* token_ids, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,6 +10,7 @@
 #include "prefill.cuh"
 #include "norm.cuh"
 #include "act.cuh"
+#include "sample.cuh"
 #include "swap.cuh"
 #include "tp_allreduce.cuh"
 #include "noalloc.cuh"

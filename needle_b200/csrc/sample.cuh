@@ -1,0 +1,394 @@
+// Batched sampler: greedy argmax and temperature / top-k / top-p draws for a
+// whole decode step in one launch.
+//
+// needle's Sampler.sample (needle/model/sampler.py:24-46) walks the batch row
+// by row with one host read per row: int(argmax) for temperature 0, otherwise
+// logit / temperature, top-k masking (logit < k-th largest -> -inf), top-p
+// masking on the descending sort (a token is removed when the probability
+// mass before it exceeds top_p), softmax and torch.multinomial.  Here one CTA
+// takes one row:
+//   * greedy rows: the first index of the maximum (NaN counts as maximal, as
+//     in torch.argmax);
+//   * sampled rows: x = round(logit / t) in the logits' dtype; the k-th
+//     largest x by an exact radix select over order-preserving integer keys
+//     (8-bit digits, most significant first); the top-p boundary by the same
+//     radix select weighted by probability mass (fp32 sums), tokens of equal
+//     value ordered by index (the order a stable descending sort gives);
+//     then one draw by inverse CDF in vocabulary order with the caller's
+//     uniform number u in [0, 1).
+// Every pass re-reads the row (256 KB at a 128k vocabulary, L2-resident after
+// the first).  Probabilities follow needle's rounding: each is rounded to the
+// logits' dtype before it enters the mass sums.
+#pragma once
+#include "nb_common.cuh"
+
+namespace nb {
+
+constexpr int kSampleThreads = 1024;
+
+template <typename T> struct SKey;
+template <> struct SKey<__nv_bfloat16> {
+  using U = uint16_t;
+  static constexpr int kBits = 16;
+  static __device__ __forceinline__ uint32_t key(__nv_bfloat16 x) {
+    const uint32_t b = __bfloat16_as_ushort(x);
+    return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  }
+};
+template <> struct SKey<__half> {
+  using U = uint16_t;
+  static constexpr int kBits = 16;
+  static __device__ __forceinline__ uint32_t key(__half x) {
+    const uint32_t b = __half_as_ushort(x);
+    return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  }
+};
+template <> struct SKey<float> {
+  using U = uint32_t;
+  static constexpr int kBits = 32;
+  static __device__ __forceinline__ uint32_t key(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  }
+};
+
+// x / t rounded to the logits' dtype (torch divides a bf16/fp16 tensor by a
+// Python float in fp32 and rounds once).
+template <typename T>
+__device__ __forceinline__ T scaled(T x, float t) {
+  return Dt<T>::from_f(__fdiv_rn(Dt<T>::to_f(x), t));
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
+  return warp_sum(s);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSampleThreads)
+    sample_kernel(const T* __restrict__ logits, int64_t stride, int V,
+                  const float* __restrict__ temperature, const int32_t* __restrict__ top_k,
+                  const float* __restrict__ top_p, const float* __restrict__ uniforms,
+                  T* __restrict__ filtered, int64_t fstride, int64_t* __restrict__ token_ids) {
+  using K = SKey<T>;
+  __shared__ float s_mass[256];
+  __shared__ unsigned s_cnt[256];
+  __shared__ float s_red[32];
+  __shared__ unsigned long long s_best;
+  __shared__ uint32_t s_key;
+  __shared__ float s_massf;
+  __shared__ unsigned s_cntf;
+  __shared__ int s_tok;
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const T* row = logits + (int64_t)r * stride;
+  const float t = temperature[r];
+
+  if (t == 0.f) {
+    // greedy: (key, ~index) maximum -> the largest value, then the smallest
+    // index; NaN maps above every number
+    unsigned long long best = 0;
+    for (int i = tid; i < V; i += blockDim.x) {
+      const T x = row[i];
+      const float f = Dt<T>::to_f(x);
+      const uint32_t k = f != f ? 0xFFFFFFFFu : K::key(x);
+      const unsigned long long c = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
+      best = c > best ? c : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long b = __shfl_xor_sync(0xffffffffu, best, o);
+      best = b > best ? b : best;
+    }
+    if (tid == 0) s_best = 0;
+    __syncthreads();
+    if ((tid & 31) == 0) atomicMax(&s_best, best);
+    __syncthreads();
+    if (tid == 0) token_ids[r] = (int64_t)(~(uint32_t)(s_best & 0xFFFFFFFFu));
+    return;
+  }
+
+  // ---- top-k: key of the k-th largest scaled logit -------------------------
+  uint32_t kth = 0;  // keep every key >= kth
+  const int kk = top_k[r];
+  if (kk > 0 && kk < V) {
+    uint32_t prefix = 0;
+    unsigned need = (unsigned)kk;  // rank still to find inside the current prefix
+    for (int shift = K::kBits - 8; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += blockDim.x) s_cnt[b] = 0;
+      __syncthreads();
+      const uint32_t hi_mask = shift + 8 >= 32 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int i = tid; i < V; i += blockDim.x) {
+        const uint32_t k = K::key(scaled(row[i], t));
+        if ((k & hi_mask) == (prefix & hi_mask)) atomicAdd(&s_cnt[(k >> shift) & 0xFF], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        unsigned acc = 0;
+        int b = 255;
+        for (; b > 0; --b) {
+          if (acc + s_cnt[b] >= need) break;
+          acc += s_cnt[b];
+        }
+        s_key = prefix | ((uint32_t)b << shift);
+        s_cntf = need - acc;
+      }
+      __syncthreads();
+      prefix = s_key;
+      need = s_cntf;
+      __syncthreads();
+    }
+    kth = prefix;
+  }
+
+  // ---- softmax over the kept tokens (fp32; each probability rounded to T) --
+  float mx = -INFINITY;
+  for (int i = tid; i < V; i += blockDim.x) {
+    const T x = scaled(row[i], t);
+    if (K::key(x) >= kth) mx = fmaxf(mx, Dt<T>::to_f(x));
+  }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) s_red[tid >> 5] = mx;
+  __syncthreads();
+  if (tid < 32) {
+    float v = tid < (int)(blockDim.x >> 5) ? s_red[tid] : -INFINITY;
+    v = warp_max(v);
+    if (tid == 0) s_massf = v;
+  }
+  __syncthreads();
+  mx = s_massf;
+  float z = 0.f;
+  for (int i = tid; i < V; i += blockDim.x) {
+    const T x = scaled(row[i], t);
+    if (K::key(x) >= kth) z += __expf(Dt<T>::to_f(x) - mx);
+  }
+  z = block_sum(z, s_red);
+  const float inv_z = 1.f / z;
+  auto prob = [&](T x) { return Dt<T>::round(__expf(Dt<T>::to_f(x) - mx) * inv_z); };
+
+  // ---- top-p: the value whose tie block holds the boundary -----------------
+  uint32_t pkey = 0;         // keep keys > pkey; of key == pkey keep the first n_tie
+  unsigned n_tie = 0xFFFFFFFFu;
+  const float pp = top_p[r];
+  const float pth = Dt<T>::round(pp);  // the comparison runs in the logits' dtype
+  if (pp < 1.f) {
+    uint32_t prefix = 0;
+    float above = 0.f;  // mass of keys above the current prefix
+    bool all_kept = false;
+    for (int shift = K::kBits - 8; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += blockDim.x) {
+        s_mass[b] = 0.f;
+        s_cnt[b] = 0;
+      }
+      __syncthreads();
+      const uint32_t hi_mask = shift + 8 >= 32 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int i = tid; i < V; i += blockDim.x) {
+        const T x = scaled(row[i], t);
+        const uint32_t k = K::key(x);
+        if (k >= kth && (k & hi_mask) == (prefix & hi_mask)) {
+          atomicAdd(&s_mass[(k >> shift) & 0xFF], prob(x));
+          atomicAdd(&s_cnt[(k >> shift) & 0xFF], 1u);
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        // the boundary bin: mass above it <= p, and its own tokens push the
+        // mass before its last token over p
+        float acc = above;
+        int b = 255;
+        bool found = false;
+        for (; b >= 0; --b) {
+          if (!s_cnt[b]) continue;
+          if (acc + s_mass[b] > pth) {
+            found = true;
+            break;
+          }
+          acc += s_mass[b];
+        }
+        s_cntf = found ? 1u : 0u;
+        s_key = found ? (prefix | ((uint32_t)b << shift)) : 0u;
+        s_massf = acc;
+      }
+      __syncthreads();
+      if (!s_cntf) {
+        all_kept = true;  // the whole remaining mass stays at or under p
+        break;
+      }
+      prefix = s_key;
+      above = s_massf;
+      __syncthreads();
+    }
+    if (!all_kept) {
+      pkey = prefix;
+      // token j (0-based, index order) of the tie block has mass `above + j p`
+      // before it; it is kept while that does not exceed p
+      T xv;  // the boundary value, decoded from its key
+      if constexpr (K::kBits == 16) {
+        const uint16_t bits =
+            (prefix & 0x8000u) ? (uint16_t)(prefix & 0x7FFFu) : (uint16_t)(~prefix & 0xFFFFu);
+        memcpy(&xv, &bits, 2);
+      } else {
+        const uint32_t bits = (prefix & 0x80000000u) ? (prefix & 0x7FFFFFFFu) : ~prefix;
+        memcpy(&xv, &bits, 4);
+      }
+      const float pv = prob(xv);
+      float slack = pth - above;
+      n_tie = pv > 0.f ? (unsigned)floorf(slack / pv) + 1u : 0xFFFFFFFFu;
+      if (slack < 0.f) n_tie = 0;
+    }
+  }
+  // kept(i): key >= kth and (key > pkey, or key == pkey and rank-in-ties < n_tie)
+  // Tie ranks need an ordered count only when the tie block is cut.
+  const bool cut = pp < 1.f && n_tie != 0xFFFFFFFFu;
+
+  // ---- draw: inverse CDF in vocabulary order over contiguous chunks ---------
+  const int chunk = (V + blockDim.x - 1) / blockDim.x;
+  const int i0 = min(V, tid * chunk), i1 = min(V, i0 + chunk);
+  // rank of this chunk's first tie token among all tie tokens (index order)
+  unsigned tie_base = 0;
+  if (cut) {
+    unsigned c = 0;
+    for (int i = i0; i < i1; ++i) c += K::key(scaled(row[i], t)) == pkey;
+    // exclusive block scan of c
+    unsigned inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, inc, o);
+      if ((tid & 31) >= o) inc += y;
+    }
+    __syncthreads();
+    if ((tid & 31) == 31) s_cnt[tid >> 5] = inc;
+    __syncthreads();
+    if (tid < 32) {
+      unsigned w = tid < (int)(blockDim.x >> 5) ? s_cnt[tid] : 0u;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, w, o);
+        if (tid >= o) w += y;
+      }
+      s_cnt[tid] = w;  // inclusive sums per warp
+    }
+    __syncthreads();
+    tie_base = inc - c + ((tid >> 5) ? s_cnt[(tid >> 5) - 1] : 0u);
+    __syncthreads();
+  }
+  auto kept = [&](uint32_t k, unsigned tie_rank) {
+    if (k < kth) return false;
+    if (pp < 1.f && n_tie != 0xFFFFFFFFu) {
+      if (k < pkey) return false;
+      if (k == pkey) return tie_rank < n_tie;
+    } else if (pp < 1.f && k < pkey) {
+      return false;
+    }
+    return true;
+  };
+  // kept mass of this chunk (unrounded exponentials of the filtered logits)
+  float csum = 0.f;
+  {
+    unsigned tr = tie_base;
+    for (int i = i0; i < i1; ++i) {
+      const T x = scaled(row[i], t);
+      const uint32_t k = K::key(x);
+      const bool kp = kept(k, tr);
+      tr += k == pkey;
+      const float e = kp ? __expf(Dt<T>::to_f(x) - mx) : 0.f;
+      csum += e;
+      if (filtered) filtered[(int64_t)r * fstride + i] = kp ? x : Dt<T>::from_f(-INFINITY);
+    }
+  }
+  // exclusive scan of the chunk sums (fp32), then the chunk holding u * total
+  float inc = csum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, inc, o);
+    if ((tid & 31) >= o) inc += y;
+  }
+  __syncthreads();
+  if ((tid & 31) == 31) s_mass[tid >> 5] = inc;
+  __syncthreads();
+  if (tid < 32) {
+    float w = tid < (int)(blockDim.x >> 5) ? s_mass[tid] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, w, o);
+      if (tid >= o) w += y;
+    }
+    s_mass[tid] = w;
+  }
+  if (tid == 0) s_tok = -1;
+  __syncthreads();
+  const float total = s_mass[(blockDim.x >> 5) - 1];
+  const float excl = inc - csum + ((tid >> 5) ? s_mass[(tid >> 5) - 1] : 0.f);
+  const float target = fminf(uniforms[r], 0.99999994f) * total;
+  if (csum > 0.f && excl <= target && target < excl + csum) {
+    float acc = excl;
+    unsigned tr = tie_base;
+    int pick = -1, last = -1;
+    for (int i = i0; i < i1; ++i) {
+      const T x = scaled(row[i], t);
+      const uint32_t k = K::key(x);
+      const bool kp = kept(k, tr);
+      tr += k == pkey;
+      if (!kp) continue;
+      last = i;
+      acc += __expf(Dt<T>::to_f(x) - mx);
+      if (acc > target) {
+        pick = i;
+        break;
+      }
+    }
+    atomicMax(&s_tok, pick >= 0 ? pick : last);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int tok = s_tok;
+    if (tok < 0) {  // rounding at the very end of the distribution: the last kept token
+      for (int i = V - 1; i >= 0; --i)
+        if (K::key(scaled(row[i], t)) >= kth) { tok = i; break; }
+    }
+    token_ids[r] = tok;
+  }
+}
+
+}  // namespace nb
+
+extern "C" {
+
+int nb_sample(const void* logits, int64_t row_stride, int num_rows, int vocab,
+              const float* temperature, const int32_t* top_k, const float* top_p,
+              const float* uniforms, void* filtered, int64_t filtered_stride,
+              int64_t* token_ids, int dtype, void* stream) {
+  using namespace nbh;
+  if (!valid_dtype(dtype)) return fail(NB_ERR_INVALID_ARG, "invalid dtype %d", dtype);
+  if (!logits || !temperature || !top_k || !top_p || !uniforms || !token_ids)
+    return fail(NB_ERR_INVALID_ARG, "null pointer argument");
+  if (num_rows < 0 || vocab <= 0) return fail(NB_ERR_INVALID_ARG, "bad sizes");
+  if (row_stride < vocab || (filtered && filtered_stride < vocab))
+    return fail(NB_ERR_INVALID_ARG, "row stride smaller than the vocabulary");
+  if (num_rows == 0) return NB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int threads = nb::kSampleThreads;
+  switch (dtype) {
+    case NB_DTYPE_F32:
+      nb::sample_kernel<float><<<num_rows, threads, 0, st>>>(
+          (const float*)logits, row_stride, vocab, temperature, top_k, top_p, uniforms,
+          (float*)filtered, filtered_stride, token_ids);
+      break;
+    case NB_DTYPE_F16:
+      nb::sample_kernel<__half><<<num_rows, threads, 0, st>>>(
+          (const __half*)logits, row_stride, vocab, temperature, top_k, top_p, uniforms,
+          (__half*)filtered, filtered_stride, token_ids);
+      break;
+    default:
+      nb::sample_kernel<__nv_bfloat16><<<num_rows, threads, 0, st>>>(
+          (const __nv_bfloat16*)logits, row_stride, vocab, temperature, top_k, top_p, uniforms,
+          (__nv_bfloat16*)filtered, filtered_stride, token_ids);
+  }
+  return check_launch("sample");
+}
+
+}  // extern "C"

@@ -15,8 +15,10 @@ device-to-host read of all the token ids:
   rows with ``top_p < 1``, one ``softmax`` and one ``multinomial`` over the
   rows.
 
-Every row-wise operation gives a row the same values as the reference's
-per-row call, so the filtered distribution each row samples from is the
+On the GPU the step runs as one kernel (``nb_sample``, see ``Sampler``); the
+torch formulation below is the host path and the documented restatement the
+kernel is tested against.  Every row-wise operation gives a row the same
+values as the reference's per-row call, so the filtered distribution each row samples from is the
 reference's (``filtered_logits`` is tested against a restatement of needle's
 loop).  The draws come from one batched ``multinomial`` instead of one call
 per row, so for a given seed the sampled ids differ from the reference's
@@ -68,7 +70,43 @@ def filtered_logits(logits: torch.Tensor, temperature: Sequence[float], top_k: S
 
 
 class Sampler:
-    """Drop-in for needle's ``Sampler`` (same ``sample`` signature)."""
+    """Drop-in for needle's ``Sampler`` (same ``sample`` signature).
+
+    On CUDA logits the whole step is one ``nb_sample`` launch (greedy rows,
+    temperature / top-k / top-p filtering and the draws) and one host read of
+    the token ids; the per-row parameters go to the device in one copy (an
+    all-greedy step reuses cached parameter arrays and copies nothing).  CPU
+    logits (host callers and tests) take the batched torch path below.
+    """
+
+    def __init__(self):
+        self._greedy = None    # device arrays for all-greedy steps
+        self._stage = None     # pinned staging of per-row parameters
+
+    def _params(self, params_list, dev, generator):
+        from .. import ops  # noqa: F401  (the library must be loadable)
+        n = len(params_list)
+        if all(p.temperature == 0.0 for p in params_list):
+            g = self._greedy
+            if g is None or g[0].numel() < n or g[0].device != dev:
+                m = max(n, 256)
+                g = (torch.zeros(m, dtype=torch.float32, device=dev),
+                     torch.zeros(m, dtype=torch.int32, device=dev),
+                     torch.ones(m, dtype=torch.float32, device=dev),
+                     torch.zeros(m, dtype=torch.float32, device=dev))
+                self._greedy = g
+            return g
+        host = torch.empty(4 * n, dtype=torch.float32).pin_memory()
+        host[:n] = torch.tensor([float(p.temperature) for p in params_list])
+        host[n:2 * n].view(torch.int32)[:] = torch.tensor(
+            [int(p.top_k) if p.top_k > 0 else 0 for p in params_list], dtype=torch.int32)
+        host[2 * n:3 * n] = torch.tensor([float(p.top_p) for p in params_list])
+        d = host.to(dev, non_blocking=True)
+        if generator is not None and generator.device.type != "cuda":
+            u = torch.rand(n, generator=generator).to(dev, non_blocking=True)
+        else:
+            u = torch.rand(n, device=dev, generator=generator)
+        return d[:n], d[n:2 * n].view(torch.int32), d[2 * n:3 * n], u
 
     @torch.no_grad()
     def sample(self, logits: torch.Tensor, params_list: Sequence,
@@ -78,6 +116,10 @@ class Sampler:
         if n == 0:
             return []
         dev = logits.device
+        if logits.is_cuda:
+            from .. import ops
+            t, k, p, u = self._params(params_list, dev, generator)
+            return ops.sample(logits, t, k, p, u).tolist()  # the step's only host read
         greedy = [p.temperature == 0.0 for p in params_list]
         ids = logits.argmax(dim=-1)
         if not all(greedy):

@@ -413,6 +413,36 @@ def swap_kv_blocks(src_caches, dst_caches, pairs: torch.Tensor) -> None:
         block_bytes, _stream(pairs)))
 
 
+def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
+           top_p: torch.Tensor, uniforms: torch.Tensor, out: Optional[torch.Tensor] = None,
+           filtered: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One token per row of ``logits [n, V]`` (``nb_sample``): greedy where
+    ``temperature == 0``, else temperature / top-k / top-p and one draw at
+    ``uniforms`` (all per-row device tensors: fp32, int32, fp32, fp32).
+    Returns int64 token ids on the device; ``filtered`` (optional, like
+    ``logits``) receives each sampled row's filtered logits."""
+    _cuda(logits, temperature, top_k, top_p, uniforms, out, filtered)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be [n, V] with unit column stride")
+    n, V = logits.shape
+    for t, dt, name in ((temperature, torch.float32, "temperature"), (top_k, torch.int32, "top_k"),
+                        (top_p, torch.float32, "top_p"), (uniforms, torch.float32, "uniforms")):
+        if t.dtype != dt or t.numel() < n or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous {dt} tensor of at least {n} rows")
+    if out is None:
+        out = torch.empty(n, dtype=torch.int64, device=logits.device)
+    if filtered is not None and (filtered.dtype != logits.dtype or filtered.shape != logits.shape
+                                 or filtered.stride(1) != 1):
+        raise ValueError("filtered must match logits' shape and dtype")
+    L.check(L.lib().nb_sample(
+        logits.data_ptr(), logits.stride(0), n, V, temperature.data_ptr(), top_k.data_ptr(),
+        top_p.data_ptr(), uniforms.data_ptr(),
+        filtered.data_ptr() if filtered is not None else None,
+        filtered.stride(0) if filtered is not None else 0, out.data_ptr(), _dtype(logits),
+        _stream(logits)))
+    return out
+
+
 def device_errors() -> int:
     """Synchronise and return (and clear) the device error word; see
     ``NB_DEVERR_*`` in the header."""

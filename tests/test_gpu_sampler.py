@@ -35,3 +35,84 @@ def test_sampler_on_device(cuda, dt):
                 continue
             # a token at the filter's boundary may flip under GPU rounding
             assert float(got[j, ids[i]]) < 1e-3, (seed, i, ids[i])
+
+
+def _kernel_rows(logits, params, dev):
+    """Run nb_sample on ``logits`` (CPU tensor) with per-row params; returns
+    (token ids, filtered logits) on the CPU."""
+    from needle_b200 import ops
+    n = logits.shape[0]
+    ld = logits.to(dev)
+    t = torch.tensor([p[0] for p in params], dtype=torch.float32, device=dev)
+    k = torch.tensor([p[1] if p[1] > 0 else 0 for p in params], dtype=torch.int32, device=dev)
+    pp = torch.tensor([p[2] for p in params], dtype=torch.float32, device=dev)
+    u = torch.rand(n, device=dev, generator=torch.Generator(device=dev).manual_seed(3))
+    filt = torch.full_like(ld, 7.0)
+    ids = ops.sample(ld, t, k, pp, u, filtered=filt)
+    assert ops.device_errors() == 0
+    return ids.cpu(), filt.cpu()
+
+
+KERNEL_PARAMS = [(0.7, 50, 1.0), (1.0, -1, 0.9), (1.3, 5, 0.5), (0.5, 0, 0.95), (2.0, 2000, 0.3),
+                 (0.9, 1, 1.0), (1.0, -1, 1.0), (0.37, 17, 0.8), (0.0, -1, 1.0)]
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_sample_kernel_keeps_needles_tokens(cuda, dt):
+    """nb_sample's filtered rows keep exactly the tokens of needle's filter
+    (oracle restatement of needle/model/sampler.py:33-46), with bit-identical
+    values, on the golden sampler case and on a case with ties at the top-k
+    boundary; the drawn token is always a kept one; greedy rows are the first
+    argmax."""
+    from tests.golden import cases as C
+    sets = [(C.sampler_inputs("bfloat16" if dt == torch.bfloat16 else "float32")["logits"],
+             C.SAMPLER_PARAMS)]
+    g = torch.Generator().manual_seed(0)
+    lg = (3 * torch.randn(len(KERNEL_PARAMS), 1000, generator=g)).to(dt)
+    lg[2, 10:20] = lg[2, 10]  # ties at the top-k boundary
+    sets.append((lg, KERNEL_PARAMS))
+    for logits, params in sets:
+        ids, filt = _kernel_rows(logits, params, cuda)
+        for i, (t, k, p) in enumerate(params):
+            if t == 0.0:
+                assert int(ids[i]) == int(logits[i].float().argmax()), i
+                continue
+            ref = no.sampler_filtered_logits(logits[i].clone(), t, k, p)
+            keep_ref, keep = torch.isfinite(ref), torch.isfinite(filt[i])
+            assert torch.equal(keep, keep_ref), (i, int((keep != keep_ref).sum()))
+            assert torch.equal(filt[i][keep], ref[keep]), i
+            assert bool(keep[ids[i]]), (i, int(ids[i]))
+
+
+def test_sample_kernel_greedy_ties_nan_and_large_vocab(cuda):
+    """Greedy rows at B=256 x V=128256 (bf16) equal torch.argmax; a row of
+    ties picks the first index; a NaN counts as the maximum."""
+    from needle_b200 import ops
+    n, V = 256, 128256
+    g = torch.Generator(device=cuda).manual_seed(5)
+    logits = torch.randn(n, V, device=cuda, generator=g).to(torch.bfloat16)
+    logits[3] = 1.0
+    logits[7, 1000] = float("nan")
+    z = torch.zeros(n, dtype=torch.float32, device=cuda)
+    ids = ops.sample(logits, z, torch.zeros(n, dtype=torch.int32, device=cuda),
+                     torch.ones(n, device=cuda), z)
+    ref = logits.argmax(dim=-1)
+    assert int(ids[3]) == 0 and int(ids[7]) == 1000
+    assert torch.equal(ids, ref)
+
+
+def test_sample_kernel_draws_follow_the_filtered_distribution(cuda):
+    """20000 draws of one row (top-k 4, top-p 0.95, temperature 0.9) match the
+    filtered softmax within sampling noise."""
+    from needle_b200 import ops
+    V, n = 6, 20000
+    row = torch.tensor([2.0, 1.0, 0.5, 0.0, -1.0, -3.0])
+    probs = torch.softmax(no.sampler_filtered_logits(row.clone(), 0.9, 4, 0.95), -1)
+    logits = row.expand(n, V).contiguous().to(cuda)
+    t = torch.full((n,), 0.9, device=cuda)
+    k = torch.full((n,), 4, dtype=torch.int32, device=cuda)
+    p = torch.full((n,), 0.95, device=cuda)
+    u = torch.rand(n, device=cuda, generator=torch.Generator(device=cuda).manual_seed(9))
+    ids = ops.sample(logits, t, k, p, u).cpu()
+    freq = torch.bincount(ids, minlength=V).float() / n
+    assert (freq - probs).abs().max() < 0.02, (freq, probs)
