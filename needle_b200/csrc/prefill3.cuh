@@ -14,7 +14,7 @@
 //     Tensor memory is allocated once per CTA, not once per unit.
 //   * Ten warps: warp 0 issues TMA loads, warp 1 issues the MMAs (one lane),
 //     warps 2-5 and 6-9 run the softmax of tiles A and B (thread = query row
-//     = TMEM lane) and the epilogue.  K and V have separate two-stage rings
+//     = TMEM lane; warp w reaches lanes 32 (w mod 4) .. +31) and the epilogue.  K and V have separate two-stage rings
 //     with their own "free" barriers: K_j is released as soon as both S MMAs
 //     that read it finish, V_j after both P.V MMAs.
 //   * A softmax thread loads its 128 scores from tensor memory with four
@@ -315,7 +315,10 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     // ---------------- softmax groups + epilogue ----------------
     const int x = (warp - 2) >> 2;  // 0 = tile A, 1 = tile B
-    const int wq = (warp - 2) & 3;  // warp quarter = TMEM lanes [32 wq, 32 wq + 32)
+    // A warp reaches the TMEM lanes of its warp index mod 4: lanes [32 wq,
+    // 32 wq + 32).  Warps 2-5 (and 6-9) are quarters 2, 3, 0, 1: each group
+    // covers all 128 lanes, and a thread's query row is its TMEM lane.
+    const int wq = warp & 3;
     const uint32_t tS = tmem + (x ? G::kSB : G::kSA);
     const uint32_t tO = tmem + (x ? G::kOB : G::kOA);
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
