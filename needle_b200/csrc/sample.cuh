@@ -25,6 +25,7 @@
 namespace nb {
 
 constexpr int kSampleThreads = 1024;
+constexpr int kBandCap = 2048;  // top-p boundary candidates sorted in shared memory
 
 template <typename T> struct SKey;
 template <> struct SKey<__nv_bfloat16> {
@@ -170,15 +171,26 @@ __global__ void __launch_bounds__(kSampleThreads)
   const float inv_z = 1.f / z;
   auto prob = [&](T x) { return Dt<T>::round(__expf(Dt<T>::to_f(x) - mx) * inv_z); };
 
-  // ---- top-p: the value whose tie block holds the boundary -----------------
-  uint32_t pkey = 0;         // keep keys > pkey; of key == pkey keep the first n_tie
+  // ---- top-p -----------------------------------------------------------------
+  // needle removes a token when round(round(S) - p) > round(top_p) in the
+  // logits' dtype, S the running fp32 sum of the rounded probabilities in
+  // descending order (torch's cumsum), p the token's own probability.  The
+  // rounding only matters within a couple of units in the last place of
+  // top_p: tokens whose mass before them lies below that band are kept, those
+  // above it removed, and the tokens in the band are sorted (value
+  // descending, index ascending: a stable sort's tie order) and scanned
+  // sequentially with those rounding points.  The result is a boundary value
+  // pkey and a tie count: keep keys > pkey and the first n_tie tokens of
+  // value pkey in index order.
+  uint32_t pkey = 0;
   unsigned n_tie = 0xFFFFFFFFu;
   const float pp = top_p[r];
   const float pth = Dt<T>::round(pp);  // the comparison runs in the logits' dtype
-  if (pp < 1.f) {
+  // the value block where the inclusive mass (from the top) first exceeds th;
+  // `above` = mass of all larger values; false if the whole mass stays <= th
+  auto select_mass = [&](float th, uint32_t& key, float& above) -> bool {
     uint32_t prefix = 0;
-    float above = 0.f;  // mass of keys above the current prefix
-    bool all_kept = false;
+    above = 0.f;
     for (int shift = K::kBits - 8; shift >= 0; shift -= 8) {
       for (int b = tid; b < 256; b += blockDim.x) {
         s_mass[b] = 0.f;
@@ -196,14 +208,12 @@ __global__ void __launch_bounds__(kSampleThreads)
       }
       __syncthreads();
       if (tid == 0) {
-        // the boundary bin: mass above it <= p, and its own tokens push the
-        // mass before its last token over p
         float acc = above;
         int b = 255;
         bool found = false;
         for (; b >= 0; --b) {
           if (!s_cnt[b]) continue;
-          if (acc + s_mass[b] > pth) {
+          if (acc + s_mass[b] > th) {
             found = true;
             break;
           }
@@ -214,31 +224,123 @@ __global__ void __launch_bounds__(kSampleThreads)
         s_massf = acc;
       }
       __syncthreads();
-      if (!s_cntf) {
-        all_kept = true;  // the whole remaining mass stays at or under p
-        break;
-      }
+      const bool found = s_cntf != 0;
       prefix = s_key;
       above = s_massf;
       __syncthreads();
+      if (!found) return false;
     }
-    if (!all_kept) {
-      pkey = prefix;
-      // token j (0-based, index order) of the tie block has mass `above + j p`
-      // before it; it is kept while that does not exceed p
-      T xv;  // the boundary value, decoded from its key
-      if constexpr (K::kBits == 16) {
-        const uint16_t bits =
-            (prefix & 0x8000u) ? (uint16_t)(prefix & 0x7FFFu) : (uint16_t)(~prefix & 0xFFFFu);
-        memcpy(&xv, &bits, 2);
-      } else {
-        const uint32_t bits = (prefix & 0x80000000u) ? (prefix & 0x7FFFFFFFu) : ~prefix;
-        memcpy(&xv, &bits, 4);
+    key = prefix;
+    return true;
+  };
+  __shared__ unsigned long long s_band[kBandCap];
+  __shared__ unsigned s_nband;
+  if (pp < 1.f) {
+    // a couple of units in the last place of top_p in the logits' dtype
+    const float ulp = fabsf(pth) * (K::kBits == 16 ? (__is_same(T, __half) ? 0x1p-10f : 0x1p-7f)
+                                                   : 0x1p-23f);
+    uint32_t kL = 0, kU = kth;
+    float aL = 0.f, aU = 0.f;
+    if (select_mass(pth - 2.f * ulp, kL, aL)) {
+      if (!select_mass(pth + 2.f * ulp, kU, aU)) kU = kth;
+      // gather the band: keys in [kU, kL]
+      if (tid == 0) s_nband = 0;
+      __syncthreads();
+      for (int i = tid; i < V; i += blockDim.x) {
+        const uint32_t k = K::key(scaled(row[i], t));
+        if (k >= kth && k >= kU && k <= kL) {
+          const unsigned slot = atomicAdd(&s_nband, 1u);
+          if (slot < (unsigned)kBandCap)
+            s_band[slot] = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
+        }
       }
-      const float pv = prob(xv);
-      float slack = pth - above;
-      n_tie = pv > 0.f ? (unsigned)floorf(slack / pv) + 1u : 0xFFFFFFFFu;
-      if (slack < 0.f) n_tie = 0;
+      __syncthreads();
+      const unsigned nb = s_nband;
+      if (nb <= (unsigned)kBandCap) {
+        // bitonic sort, descending, over the next power of two (pads sort last)
+        unsigned n2 = 1;
+        while (n2 < nb) n2 <<= 1;
+        for (unsigned i = nb + tid; i < n2; i += blockDim.x) s_band[i] = 0ull;
+        __syncthreads();
+        for (unsigned size = 2; size <= n2; size <<= 1)
+          for (unsigned stride = size >> 1; stride > 0; stride >>= 1) {
+            for (unsigned i = tid; i < n2; i += blockDim.x) {
+              const unsigned j = i ^ stride;
+              if (j > i) {
+                const unsigned long long a = s_band[i], b = s_band[j];
+                const bool desc = (i & size) == 0;
+                if (desc ? a < b : a > b) {
+                  s_band[i] = b;
+                  s_band[j] = a;
+                }
+              }
+            }
+            __syncthreads();
+          }
+        if (tid == 0) {
+          // sequential scan with needle's rounding points
+          float S = aL;
+          uint32_t cur = 0xFFFFFFFFu;
+          unsigned rank = 0;
+          uint32_t bkey = 0;
+          unsigned btie = 0xFFFFFFFFu;
+          bool cut = false;
+          for (unsigned c = 0; c < nb; ++c) {
+            const uint32_t k = (uint32_t)(s_band[c] >> 32);
+            if (k != cur) {
+              cur = k;
+              rank = 0;
+            }
+            T xv;
+            if constexpr (K::kBits == 16) {
+              const uint16_t bits =
+                  (k & 0x8000u) ? (uint16_t)(k & 0x7FFFu) : (uint16_t)(~k & 0xFFFFu);
+              memcpy(&xv, &bits, 2);
+            } else {
+              const uint32_t bits = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+              memcpy(&xv, &bits, 4);
+            }
+            const float pv = prob(xv);
+            S = __fadd_rn(S, pv);
+            const float d = Dt<T>::round(__fsub_rn(Dt<T>::round(S), pv));
+            if (d > pth) {
+              bkey = k;
+              btie = rank;
+              cut = true;
+              break;
+            }
+            ++rank;
+          }
+          if (!cut) {  // every band token kept: the cut is right below the band
+            bkey = kU;
+            btie = 0xFFFFFFFFu;
+          }
+          s_key = bkey;
+          s_cntf = btie;
+        }
+        __syncthreads();
+        pkey = s_key;
+        n_tie = s_cntf;
+        __syncthreads();
+      } else {
+        // band too wide to sort here: the fp32 criterion (mass before <= top_p)
+        uint32_t kb;
+        float ab;
+        if (select_mass(pth, kb, ab)) {
+          pkey = kb;
+          T xv;
+          if constexpr (K::kBits == 16) {
+            const uint16_t bits =
+                (kb & 0x8000u) ? (uint16_t)(kb & 0x7FFFu) : (uint16_t)(~kb & 0xFFFFu);
+            memcpy(&xv, &bits, 2);
+          } else {
+            const uint32_t bits = (kb & 0x80000000u) ? (kb & 0x7FFFFFFFu) : ~kb;
+            memcpy(&xv, &bits, 4);
+          }
+          const float pv = prob(xv);
+          n_tie = pv > 0.f ? (unsigned)floorf((pth - ab) / pv) + 1u : 0xFFFFFFFFu;
+        }
+      }
     }
   }
   // kept(i): key >= kth and (key > pkey, or key == pkey and rank-in-ties < n_tie)

@@ -57,13 +57,33 @@ KERNEL_PARAMS = [(0.7, 50, 1.0), (1.0, -1, 0.9), (1.3, 5, 0.5), (0.5, 0, 0.95), 
                  (0.9, 1, 1.0), (1.0, -1, 1.0), (0.37, 17, 0.8), (0.0, -1, 1.0)]
 
 
+def _needle_rule_stable(logit, t, k, p):
+    """needle's filter (needle/model/sampler.py:33-46, as oracle.needle_oracle
+    restates it) with a stable descending sort: tokens of equal value in
+    index order.  needle's own sort is unstable on the CPU, so which tokens of
+    a value tied exactly at the top-p boundary it keeps is unspecified; the
+    kernel fixes index order (what a stable sort, and the GPU sort, give)."""
+    logit = logit / t
+    if k > 0:
+        kth = logit.topk(min(k, logit.size(-1))).values[-1]
+        logit = logit.masked_fill(logit < kth, float("-inf"))
+    if p < 1.0:
+        sl, si = logit.sort(descending=True, stable=True)
+        cum = sl.softmax(dim=-1).cumsum(dim=-1)
+        remove = cum - sl.softmax(dim=-1) > p
+        sl[remove] = float("-inf")
+        logit = logit.scatter(0, si, sl)
+    return logit
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 def test_sample_kernel_keeps_needles_tokens(cuda, dt):
     """nb_sample's filtered rows keep exactly the tokens of needle's filter
-    (oracle restatement of needle/model/sampler.py:33-46), with bit-identical
-    values, on the golden sampler case and on a case with ties at the top-k
-    boundary; the drawn token is always a kept one; greedy rows are the first
-    argmax."""
+    (needle/model/sampler.py:33-46) with ties in index order, with
+    bit-identical values, on the golden sampler case and on a case with ties
+    at the top-k boundary; against needle's unstable-sort oracle the kept
+    count is equal and any difference lies inside one tie block; the drawn
+    token is always a kept one; greedy rows are the first argmax."""
     from tests.golden import cases as C
     sets = [(C.sampler_inputs("bfloat16" if dt == torch.bfloat16 else "float32")["logits"],
              C.SAMPLER_PARAMS)]
@@ -77,11 +97,17 @@ def test_sample_kernel_keeps_needles_tokens(cuda, dt):
             if t == 0.0:
                 assert int(ids[i]) == int(logits[i].float().argmax()), i
                 continue
-            ref = no.sampler_filtered_logits(logits[i].clone(), t, k, p)
+            ref = _needle_rule_stable(logits[i].clone(), t, k, p)
             keep_ref, keep = torch.isfinite(ref), torch.isfinite(filt[i])
             assert torch.equal(keep, keep_ref), (i, int((keep != keep_ref).sum()))
             assert torch.equal(filt[i][keep], ref[keep]), i
             assert bool(keep[ids[i]]), (i, int(ids[i]))
+            nd = torch.isfinite(no.sampler_filtered_logits(logits[i].clone(), t, k, p))
+            assert int(nd.sum()) == int(keep.sum()), i
+            diff = (nd != keep).nonzero().flatten()
+            if diff.numel():
+                x = logits[i][diff] / t
+                assert bool((x == x[0]).all()), (i, diff)
 
 
 def test_sample_kernel_greedy_ties_nan_and_large_vocab(cuda):
