@@ -646,10 +646,10 @@ int launch_prefill_tc2(const void* q, int64_t qs, const void* k, int64_t ks, con
 
 inline int prefill_version() {
   static int v = [] {
-    // "1": single-group kernel, "3": the persistent kernel (prefill3.cuh);
-    // default: the per-unit two-group kernel
+    // "1": single-group kernel, "2": per-unit two-group kernel (diagnostics);
+    // default: the persistent kernel (prefill3.cuh)
     const char* e = getenv("NB_PREFILL_V");
-    return (e && e[0] == '1') ? 1 : (e && e[0] == '3') ? 3 : 2;
+    return (e && e[0] == '1') ? 1 : (e && e[0] == '2') ? 2 : 3;
   }();
   return v;
 }

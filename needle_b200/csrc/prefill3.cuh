@@ -60,6 +60,30 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 2^x on the FMA/ALU pipes, for the share of the softmax exponentials that
+// would otherwise queue on the MUFU (XU) pipe, which limits this kernel.
+// Cody-Waite style range reduction: n = round(x) through the 1.5 * 2^23 magic
+// constant, f = x - n in [-0.5, 0.5]; 2^f by a cubic whose coefficients were
+// fit here (least squares weighted by relative error on [-0.5, 0.5], maximum
+// relative error 1.0e-4, below half a unit of bf16 and fp16); 2^n is added to
+// the exponent field.  Valid for x >= -126 (the unmasked scores, which are at
+// most a few units above the running max).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+  float p = fmaf(0.05500858144334074f, f, 0.24221037434204812f);
+  p = fmaf(p, f, 0.6932829004942702f);
+  p = fmaf(p, f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Exponentials per group of 8 value pairs that take exp2_poly instead of
+// the MUFU in unmasked tiles.
+#ifndef NB_PF3_POLY
+#define NB_PF3_POLY 3
+#endif
+
 template <int D> struct Pf3Geom {
   static constexpr int kAtom = 128 * 128;       // 128 rows x 128 B
   static constexpr int kTile = (D / 64) * kAtom;
@@ -380,11 +404,19 @@ __global__ void __launch_bounds__(320, 1)
             uint32_t pk[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              // masked scores are -inf: exp2 gives exactly 0
+              // masked scores are -inf: the MUFU's exp2 gives exactly 0, so
+              // masked tiles use it for every value
               const int i = hh * 16 + 2 * e;
-              const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c][i]), scale_log2, neg_m));
-              const float p1 =
-                  ex2_approx(fmaf(__uint_as_float(sr[c][i + 1]), scale_log2, neg_m));
+              const float x0 = fmaf(__uint_as_float(sr[c][i]), scale_log2, neg_m);
+              const float x1 = fmaf(__uint_as_float(sr[c][i + 1]), scale_log2, neg_m);
+              float p0, p1;
+              if (e < NB_PF3_POLY && full) {
+                p0 = exp2_poly(x0);
+                p1 = exp2_poly(x1);
+              } else {
+                p0 = ex2_approx(x0);
+                p1 = ex2_approx(x1);
+              }
               rs += p0 + p1;
               pk[e] = Mma<T>::pack(p0, p1);
             }
