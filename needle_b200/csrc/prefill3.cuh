@@ -81,7 +81,7 @@ __device__ __forceinline__ float exp2_poly(float x) {
 // Exponentials per group of 8 value pairs that take exp2_poly instead of
 // the MUFU in unmasked tiles.
 #ifndef NB_PF3_POLY
-#define NB_PF3_POLY 3
+#define NB_PF3_POLY 0
 #endif
 
 template <int D> struct Pf3Geom {
@@ -372,22 +372,24 @@ __global__ void __launch_bounds__(320, 1)
         const int kb = j * 128;
         // whole tile below the diagonal and inside the sequence: no masking
         const bool full = kb + 127 <= qi && kb + 128 <= len;
-        float mx = -INFINITY;
-        if (full) {
+        // row max over 8 independent accumulators (no 128-deep dependency)
+        float mxa[8];
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[c][i]));
-        } else {
+        for (int a = 0; a < 8; ++a) mxa[a] = -INFINITY;
+        if (!full) {
           const int lim = min(qi, len - 1) - kb;  // last visible column of the row
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < 32; ++i)
               if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
-              mx = fmaxf(mx, __uint_as_float(sr[c][i]));
-            }
         }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], __uint_as_float(sr[c][i]));
+        float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                         fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
         mx *= scale_log2;  // scale > 0: max of scaled scores = scaled max
         const bool need = mx > m + kRescaleThreshold;
         float alpha = 1.f;
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(320, 1)
           m = mx;
         }
         const float neg_m = -m;
-        float rs = 0.f;
+        float rsa[4] = {0.f, 0.f, 0.f, 0.f};  // row sum in 4 independent partials
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
 #pragma unroll
@@ -417,12 +419,13 @@ __global__ void __launch_bounds__(320, 1)
                 p0 = ex2_approx(x0);
                 p1 = ex2_approx(x1);
               }
-              rs += p0 + p1;
+              rsa[e & 3] += p0 + p1;
               pk[e] = Mma<T>::pack(p0, p1);
             }
             tmem_st8(tS + lane_off + c * 16 + hh * 8, pk);  // P over S's first 64 columns
           }
         }
+        const float rs = (rsa[0] + rsa[1]) + (rsa[2] + rsa[3]);
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // rescale O_X (P_X(j-1).V_{j-1} is complete: the commit that
           // signalled S_X(j) covers it; P_X(j).V_j waits for this group's
