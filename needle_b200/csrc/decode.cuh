@@ -1,7 +1,8 @@
 // Paged split-K decode attention and its merge kernel.
 //
-// Tensor-core path (bf16/fp16, block_size 16, head_dim 64/128, group <= 8):
-//   * one CTA of WARPS warps per (split, kv head, sequence); a split is a run of
+// Tensor-core path (bf16/fp16, block_size 16, head_dim 64/128, any group):
+//   * one CTA of WARPS warps per (split, kv head, chunk of <= 8 query heads of
+//     its group, sequence); a split is a run of
 //     `pps` consecutive pages (KV blocks) of the sequence;
 //   * warp w owns pages w, w+WARPS, ... of its split and runs its own
 //     STAGES-deep TMA pipeline: each 16-token page of K and of V lands in a
@@ -77,9 +78,15 @@ __global__ void __launch_bounds__(WARPS * 32)
                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // grid.y = kv head x chunks of up to 8 query heads of its group: groups
+  // above 8 run as several CTAs that read the same pages (adjacent in the
+  // grid, so the second read of a page is usually an L2 hit)
+  const int nhc = (group + 7) >> 3;
+  const int split = blockIdx.x, h = blockIdx.y / nhc, b = blockIdx.z;
+  const int n0 = (blockIdx.y - h * nhc) * 8;
+  const int gcount = min(8, group - n0);
   const int ctx = __ldg(ctx_lens + b);
-  if (ctx < 0 && threadIdx.x == 0 && split == 0) set_error(kErrPosition);
+  if (ctx < 0 && threadIdx.x == 0 && split == 0 && n0 == 0) set_error(kErrPosition);
   int n_tok, n_pages, n_splits;
   decode_extent(ctx, maxb, 16, pps, n_tok, n_pages, n_splits);
   if (split >= n_splits) return;
@@ -132,8 +139,8 @@ __global__ void __launch_bounds__(WARPS * 32)
   // Q^T as the B operand (k = d, n = head): lane holds heads g, d pairs 2*t4.
   uint32_t qf[NK][2];
   {
-    const bool hv = g < group;
-    const T* qrow = q + (int64_t)b * q_sb + (int64_t)(h * group + (hv ? g : 0)) * q_sh;
+    const bool hv = g < gcount;
+    const T* qrow = q + (int64_t)b * q_sb + (int64_t)(h * group + n0 + (hv ? g : 0)) * q_sh;
 #pragma unroll
     for (int kk = 0; kk < NK; ++kk) {
       qf[kk][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4)) : 0u;
@@ -254,7 +261,7 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
   __syncthreads();
   const int H = kvh * group;
-  for (int idx = threadIdx.x; idx < group * D; idx += WARPS * 32) {
+  for (int idx = threadIdx.x; idx < gcount * D; idx += WARPS * 32) {
     const int n = idx / D, d = idx - n * D;
     float M = -INFINITY;
 #pragma unroll
@@ -267,7 +274,7 @@ __global__ void __launch_bounds__(WARPS * 32)
       L += sm_l[w * 8 + n] * e;
       O += sm_o[(w * 8 + n) * D + d] * e;
     }
-    const int qh = h * group + n;
+    const int qh = h * group + n0 + n;
     if (n_splits == 1) {
       out[(int64_t)b * o_sb + (int64_t)qh * o_sh + d] = Dt<T>::from_f(L > 0.f ? O / L : 0.f);
     } else {
@@ -523,7 +530,8 @@ int launch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t
   if (int rc = ensure_max_smem((const void*)kern, (int)smem, "paged_decode_tc")) return rc;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
-  pdl_config(cfg, attr, dim3(max_splits, kvh, B), dim3(WARPS * 32), smem, st);
+  pdl_config(cfg, attr, dim3(max_splits, kvh * ((group + 7) / 8), B), dim3(WARPS * 32), smem,
+             st);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, map, (const T*)q, qsb, qsh, bt, bts, maxb,
                                            ctx, kvh, group, nblk, scale_log2, pps, (T*)out, osb,
                                            osh, po, pml, max_splits);
@@ -682,7 +690,7 @@ int nb_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t rows = 2ll * num_blocks * num_kv_heads * block_size;
   const bool tc = dtype != NB_DTYPE_F32 && block_size == 16 &&
-                  (head_dim == 64 || head_dim == 128) && group <= 8 &&
+                  (head_dim == 64 || head_dim == 128) &&
                   pages_per_split <= max_pages_per_split_tc() && rows < (1ll << 31) &&
                   (uintptr_t)kv_cache % 16 == 0 && (uintptr_t)q % 4 == 0 &&
                   q_stride_seq % 2 == 0 && q_stride_head % 2 == 0;

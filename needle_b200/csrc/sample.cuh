@@ -90,16 +90,49 @@ __global__ void __launch_bounds__(kSampleThreads)
   const float t = temperature[r];
 
   if (t == 0.f) {
-    // greedy: (key, ~index) maximum -> the largest value, then the smallest
-    // index; NaN maps above every number
-    unsigned long long best = 0;
-    for (int i = tid; i < V; i += blockDim.x) {
-      const T x = row[i];
+    // greedy: the largest ordered key, then the smallest index; NaN maps
+    // above every number.  A thread visits its indices in increasing order,
+    // so a strictly larger key is the only update it needs.
+    uint32_t bk = 0;
+    int bi = 0x7FFFFFFF;
+    constexpr int VEC = 16 / sizeof(T);
+    auto visit = [&](T x, int i) {
       const float f = Dt<T>::to_f(x);
       const uint32_t k = f != f ? 0xFFFFFFFFu : K::key(x);
-      const unsigned long long c = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
-      best = c > best ? c : best;
+      if (k > bk || bi == 0x7FFFFFFF) {
+        bk = k;
+        bi = i;
+      }
+    };
+    if (((uintptr_t)row & 15) == 0) {
+      // 16-byte vectors, four in flight per thread
+      const int nv = V / VEC;
+      const uint4* rv = reinterpret_cast<const uint4*>(row);
+      for (int v0 = tid; v0 < nv; v0 += 4 * blockDim.x) {
+        uint4 buf[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int v = v0 + u * blockDim.x;
+          if (v < nv) buf[u] = __ldg(rv + v);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int v = v0 + u * blockDim.x;
+          if (v < nv) {
+            const T* xs = reinterpret_cast<const T*>(&buf[u]);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) visit(xs[e], v * VEC + e);
+          }
+        }
+      }
+      for (int i = nv * VEC + tid; i < V; i += blockDim.x) visit(row[i], i);
+    } else {
+      for (int i = tid; i < V; i += blockDim.x) visit(row[i], i);
     }
+    // (key, ~index): the block maximum is the largest key at the smallest index
+    unsigned long long best =
+        bi == 0x7FFFFFFF ? 0ull
+                         : ((unsigned long long)bk << 32) | (uint32_t)(~(uint32_t)bi);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long b = __shfl_xor_sync(0xffffffffu, best, o);

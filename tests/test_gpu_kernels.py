@@ -246,9 +246,11 @@ def test_decode_vs_needle_golden(cuda, dt, H, kv, D, pps):
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("H,kv,D", [(32, 8, 128), (14, 2, 64), (64, 8, 128), (16, 1, 128),
-                                    (8, 8, 128), (12, 4, 96)])
+                                    (8, 8, 128), (12, 4, 96), (48, 2, 128), (20, 1, 64)])
 def test_decode_random_shapes(cuda, dt, H, kv, D):
-    """Group sizes 4, 7, 8, 16 (beyond one MMA tile), MHA and an odd head_dim."""
+    """Group sizes 4, 7, 8, 16, 24 and 20 (beyond one MMA tile: the tensor-core
+    kernel takes 8 query heads per CTA, the last chunk partial), MHA and an
+    odd head_dim."""
     ops = _ops()
     g = torch.Generator().manual_seed(15)
     B, N, maxb = 9, 400, 40
