@@ -22,19 +22,25 @@ _saved = {}
 
 
 def patch_needle() -> None:
-    """Route ``needle.layers.attention.Attention.forward`` and
-    ``needle.layers.norm.RMSNorm.forward`` to this library."""
+    """Route ``needle.layers.attention.Attention.forward``,
+    ``needle.layers.norm.RMSNorm.forward`` and ``needle.model.sampler.Sampler.sample``
+    (same signature; CUDA logits take one ``nb_sample`` launch per step) to
+    this library."""
     importlib.import_module("needle")
     importlib.import_module("needle.model")  # needle.layers.attention alone is a circular import
     attn_mod = importlib.import_module("needle.layers.attention")
     norm_mod = importlib.import_module("needle.layers.norm")
+    samp_mod = importlib.import_module("needle.model.sampler")
     from .layers.attention import Attention
     from .layers.norm import RMSNorm
+    from .model.sampler import Sampler
     if not _saved:
         _saved["attn"] = attn_mod.Attention.forward
         _saved["norm"] = norm_mod.RMSNorm.forward
+        _saved["sample"] = samp_mod.Sampler.sample
     attn_mod.Attention.forward = Attention.forward
     norm_mod.RMSNorm.forward = RMSNorm.forward
+    samp_mod.Sampler.sample = Sampler.sample
 
 
 def unpatch_needle() -> None:
@@ -42,5 +48,7 @@ def unpatch_needle() -> None:
         return
     attn_mod = importlib.import_module("needle.layers.attention")
     norm_mod = importlib.import_module("needle.layers.norm")
+    samp_mod = importlib.import_module("needle.model.sampler")
     attn_mod.Attention.forward = _saved.pop("attn")
     norm_mod.RMSNorm.forward = _saved.pop("norm")
+    samp_mod.Sampler.sample = _saved.pop("sample")

@@ -87,7 +87,8 @@ class Sampler:
         from .. import ops  # noqa: F401  (the library must be loadable)
         n = len(params_list)
         if all(p.temperature == 0.0 for p in params_list):
-            g = self._greedy
+            # getattr: patch_needle() binds this method to needle's own Sampler
+            g = getattr(self, "_greedy", None)
             if g is None or g[0].numel() < n or g[0].device != dev:
                 m = max(n, 256)
                 g = (torch.zeros(m, dtype=torch.float32, device=dev),

@@ -40,13 +40,19 @@ class _NeedleRMSNorm(nn.Module):
         return "needle norm"
 
 
+class _NeedleSampler:
+    def sample(self, logits, sampling_params_list):
+        return "needle sampler"
+
+
 @pytest.fixture
 def fake_needle(monkeypatch):
     mods = {name: types.ModuleType(name) for name in
             ("needle", "needle.model", "needle.layers", "needle.layers.attention",
-             "needle.layers.norm")}
+             "needle.layers.norm", "needle.model.sampler")}
     mods["needle.layers.attention"].Attention = _NeedleAttention
     mods["needle.layers.norm"].RMSNorm = _NeedleRMSNorm
+    mods["needle.model.sampler"].Sampler = _NeedleSampler
     for name, m in mods.items():
         monkeypatch.setitem(sys.modules, name, m)
     yield
@@ -71,5 +77,10 @@ def test_patch_routes_needle_modules_to_the_library(fake_needle):
         norm(x)
     with pytest.raises(ValueError, match="CUDA"):
         norm(x, x.clone())
+    # the sampler takes needle's signature; on CPU logits it runs the host path
+    from needle_b200.model.sequence import SamplingParams
+    ids = _NeedleSampler().sample(torch.tensor([[0.1, 2.0, -1.0]]), [SamplingParams(temperature=0.0)])
+    assert ids == [1]
     unpatch_needle()
     assert attn(x) == "needle attention" and norm(x) == "needle norm"
+    assert _NeedleSampler().sample(None, []) == "needle sampler"
