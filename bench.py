@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample budget (rank 0, N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-shape", default="16x1024",
+                    help="prefill workload: sequences x new tokens per sequence")
     ap.add_argument("--workload",
                     choices=["llama8b", "llama8b-c4", "qwen72b", "decode-op", "prefill",
                              "allreduce", "store-kv", "kernel-cases"],
@@ -857,14 +859,15 @@ def _splits(runner, seqs) -> int:
 # ---------------------------------------------------------------------------
 
 def run_prefill(args):
-    """Causal prefill attention of 16 sequences x 1024 new tokens, 32/8 heads,
-    D=128, bf16 (the config 3 head geometry); reports TFLOP/s against the
-    measured dense bf16 peak."""
+    """Causal prefill attention of ``--prefill-shape`` (default 16 sequences x
+    1024 new tokens), 32/8 heads, D=128, bf16 (the config 3 head geometry);
+    reports TFLOP/s against the measured dense bf16 peak."""
     rank, local, ws = dist_init(args.gpus)
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
     from needle_b200 import ops
-    B, S, H, KV, D = 16, 1024, 32, 8, 128
+    B, S = (int(v) for v in args.prefill_shape.lower().split("x"))
+    H, KV, D = 32, 8, 128
     g = torch.Generator(device=dev).manual_seed(0)
     T = B * S
     q = torch.randn(T, H, D, device=dev, generator=g, dtype=torch.bfloat16)
@@ -901,7 +904,7 @@ def run_prefill(args):
             "unit": "TFLOP/s", "n_gpus": ws, "steps": K, "warmup": max(3, args.warmup),
             "ms_per_step": round(t_ms / K, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,1))",
-            "config": {"workload": "prefill: 16 x 1024 new tokens, 32/8 heads, D=128, causal"},
+            "config": {"workload": f"prefill: {B} x {S} new tokens, 32/8 heads, D=128, causal"},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
                          "peak_source": src, "flops_per_call": flops, "traffic": None},

@@ -32,7 +32,12 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int e = 0; e < VEC; ++e) {
     const float x = Dt<T>::to_f(gv[e]);
-    const float s = Dt<T>::round(x / (1.0f + expf(-x)));
+    // silu in fp32 with the fast exponential and divide: a few fp32 ulps from
+    // torch's x / (1 + exp(-x)), below the bf16/fp16 rounding that follows
+    // (fp32 itself keeps the exact forms)
+    float s;
+    if constexpr (sizeof(T) == 2) s = Dt<T>::round(__fdividef(x, 1.0f + __expf(-x)));
+    else s = x / (1.0f + expf(-x));
     ov[e] = Dt<T>::from_f(s * Dt<T>::to_f(uv[e]));
   }
   T* o = out + t * out_stride + c;

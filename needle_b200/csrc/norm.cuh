@@ -25,6 +25,53 @@ __global__ void __launch_bounds__(1024)
   T* hr = ADD ? res_out + (int64_t)row * ros : nullptr;
   T* orow = out + (int64_t)row * os;
   const int nvec = hidden / VEC;
+  if (VEC * sizeof(T) == 16 && nvec <= (int)blockDim.x) {
+    // One vector per thread (every decode shape up to hidden 8192): the row
+    // stays in registers between the two passes and the weight load is
+    // issued with the first loads, so the kernel makes one memory round trip.
+    const int i = threadIdx.x;
+    const bool mine = i < nvec;
+    T hv[VEC], wv[VEC];
+    float ss = 0.f;
+    if (mine) {
+      *reinterpret_cast<uint4*>(hv) = *reinterpret_cast<const uint4*>(xr + i * VEC);
+      *reinterpret_cast<uint4*>(wv) = __ldg(reinterpret_cast<const uint4*>(w + i * VEC));
+      if constexpr (ADD) {
+        T rv[VEC];
+        *reinterpret_cast<uint4*>(rv) = *reinterpret_cast<const uint4*>(rr + i * VEC);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          hv[e] = Dt<T>::from_f(__fadd_rn(Dt<T>::to_f(rv[e]), Dt<T>::to_f(hv[e])));
+        *reinterpret_cast<uint4*>(hr + i * VEC) = *reinterpret_cast<uint4*>(hv);
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float f = Dt<T>::to_f(hv[e]);
+        ss = __fadd_rn(ss, __fmul_rn(f, f));
+      }
+    }
+    ss = warp_sum(ss);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+      float v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+      v = warp_sum(v);
+      if (lane == 0) red[0] = v;
+    }
+    __syncthreads();
+    if (mine) {
+      const float var = __fdiv_rn(red[0], (float)hidden);
+      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float xn = Dt<T>::round(__fmul_rn(Dt<T>::to_f(hv[e]), r));
+        hv[e] = Dt<T>::from_f(__fmul_rn(Dt<T>::to_f(wv[e]), xn));
+      }
+      *reinterpret_cast<uint4*>(orow + i * VEC) = *reinterpret_cast<uint4*>(hv);
+    }
+    return;
+  }
   float ss = 0.f;
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     T hv[VEC];

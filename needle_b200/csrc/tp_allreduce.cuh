@@ -31,18 +31,22 @@
 //     rank's results of the call in between, which this rank sent after it
 //     had consumed (and reset) the half being rewritten.
 //
-// Memory ordering (PTX memory model, system scope).  Every access that
-// another GPU can observe is strong: pushes and sentinel resets are
-// st.relaxed.sys, polls are ld.relaxed.sys.  A thread executes
-// fence.acq_rel.sys (a) before its first push of a call, (b) after its
-// receive polls and before its gather pushes, and (c) after its gather polls
-// and resets.  Each push is therefore a release and each successful poll,
-// followed by (b) or (c), an acquire, so the hand-off "rank A resets slot X,
-// then pushes; rank B observes that push (directly, or through rank 0's
-// gather, which every rank receives for every row index), then writes X"
-// puts A's reset before B's write in X's coherence order: a late reset can
-// never overwrite new data.  Consecutive launches on one stream are ordered
-// by the stream, which carries the chain from one call to the next.
+// Memory ordering.  Every access another GPU can observe is strong
+// (ld.relaxed.sys polls, st.relaxed.sys pushes and sentinel resets), and the
+// data is its own arrival signal per 16-bit lane, so no data word needs to be
+// ordered before another.  The one hazard is a late sentinel reset: rank A
+// resets slot X (in its own memory) after consuming it, and sender B writes X
+// again two calls later; the reset must not land after B's new data.  A
+// thread resets its consumed slots only after it has issued all of its pushes
+// of the call, so B's next write to X is causally after a push that A makes
+// in a LATER launch (B's call two steps on waits, directly or through rank 0's
+// gather that every rank receives, for data that A pushed in the call in
+// between).  Launches on one stream are ordered: A's later launch starts
+// only after every store of the earlier one has been performed at A's L2,
+// which is also where B's NVLink store to X lands (the point of coherence of
+// A's memory).  So B's write is ordered after A's reset in X's coherence
+// order, without any fence in the kernel; a reader never acts on a slot
+// before its own poll returned the data (no speculative stores).
 //
 // Failure: every wait is bounded (nb_tp_set_wait_limit_ns, 2 s by default).
 // A CTA that gives up records NB_DEVERR_TIMEOUT, sets the communicator's
@@ -88,23 +92,6 @@ __device__ __forceinline__ void st_relaxed_sys_v4(void* p, const uint4& v) {
                "r"(v.z), "r"(v.w)
                : "memory");
 }
-__device__ __forceinline__ void fence_acq_rel_sys() {
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-}
-#ifndef NB_AR_FENCE_MASK
-#define NB_AR_FENCE_MASK 7
-#endif
-#ifndef NB_AR_FENCE_GPU
-#define NB_AR_FENCE_GPU 0
-#endif
-template <int BIT>
-__device__ __forceinline__ void ar_fence() {
-  if constexpr ((NB_AR_FENCE_MASK & BIT) != 0) {
-    if constexpr (NB_AR_FENCE_GPU) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    else fence_acq_rel_sys();
-  }
-}
-
 __device__ __forceinline__ bool lane_is_sentinel(unsigned w) {
   return (w & 0xFFFFu) == 0xFFFFu || (w >> 16) == 0xFFFFu;
 }
@@ -200,9 +187,6 @@ __global__ void __launch_bounds__(1024)
       s_e = ep[b];
       s_poison = *status;
     }
-    // (a) release: everything before this call (earlier launches' resets
-    // included, through stream order) is ordered before this call's pushes
-    ar_fence<1>();
     // owners q with a row at index b: q*per+b < rows
     const int nq = min(world, (rows - 1 - b) / per + 1);
     if (role == 0) {
@@ -286,8 +270,6 @@ __global__ void __launch_bounds__(1024)
           // A thread whose wait ran out pushes nothing more, so every rank
           // that needs its rows times out as well instead of reading garbage.
           if (!dead) {
-            // (b) acquire the receive polls, release before the gather pushes
-            ar_fence<2>();
 #pragma unroll
             for (int p = 0; p < MAXW; ++p) {
               if (p < world) {
@@ -296,8 +278,8 @@ __global__ void __launch_bounds__(1024)
                 st_relaxed_sys_v4(gp + hidden, o4);
               }
             }
-            // the consumed receive slots, reset off the critical path (they
-            // are written again two calls later, after (a) of a later launch)
+            // the consumed receive slots, reset after this call's pushes (they
+            // are written again two calls later, after a later launch)
             reset_vecs<MAXW>(rb, slot, world);
           }
         }
@@ -343,9 +325,6 @@ __global__ void __launch_bounds__(1024)
         }
       }
     }
-    // (c) acquire the gather polls: what a peer did before its gather push is
-    // ordered before this rank's next pushes
-    ar_fence<4>();
     if (__syncthreads_or(dead)) {
       if (threadIdx.x == 0) {
         set_error(kErrTimeout);
