@@ -665,10 +665,16 @@ def run_model(args):
             prefill_seqs=[], decode_seqs=seqs, block_tables=drv.tables, swap_in_map={},
             swap_out_map={}, blocks_to_free=[]))
         merges = _splits(runner, seqs) > 1
+        from needle_b200 import ops
+        greedy = (torch.zeros(B, dtype=torch.float32, device=dev),
+                  torch.zeros(B, dtype=torch.int32, device=dev),
+                  torch.ones(B, dtype=torch.float32, device=dev),
+                  torch.zeros(B, dtype=torch.float32, device=dev))
 
         def device_step():
             logits = runner._forward(inp)
-            torch.argmax(logits, dim=-1, out=inp.input_ids)
+            # greedy tokens (the sampler kernel) straight into the next step's ids
+            ops.sample(logits, *greedy, out=inp.input_ids)
             inp.position_ids.add_(1)
             inp.context_lens.add_(1)
         device_step()                    # untimed: the graph of this width is warm
@@ -725,7 +731,8 @@ def run_model(args):
                        "parallelism": f"tp{ws}" if ws > 1 else "single GPU",
                        "l2": "inputs larger than L2 (%.1f GB of weights read per step)"
                              % (w_bytes / 1e9),
-                       "value_loop": "decode graph replays, greedy token fed back on device",
+                       "value_loop": "decode graph replays, greedy token (sampler kernel) fed "
+                                     "back on the device",
                        "allreduce": (None if ws == 1 else allreduce["kind"])},
             "roofline": kern["roofline"],
             "step_roofline": {"bound": "hbm", "what": "whole decode step per rank: weights + "
@@ -743,10 +750,12 @@ def run_model(args):
                             "copied from pinned memory, token ids read back every step",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": B * 8},
             "cpu_baseline": None,  # filled in below, after the process group is gone
-            # our kernels per decode step: the first RMSNorm, per layer the
-            # RoPE + KV write, paged decode (+ merge when split), two fused
-            # add+RMSNorm (fused all-reduce under TP) and SwiGLU
-            "gpu_launches": Kd * (cfg.num_hidden_layers * (5 + (1 if merges else 0)) + 1),
+            # our kernels per decode step: the slot table, the first RMSNorm,
+            # per layer the RoPE + KV write, paged decode (+ merge when split),
+            # SwiGLU and two fused add+RMSNorm (post-attention, and the next
+            # layer's input norm or the final norm; the fused all-reduce under
+            # TP), and the sampler
+            "gpu_launches": Kd * (cfg.num_hidden_layers * (5 + (1 if merges else 0)) + 3),
             "clocks": clocks.summary(),
         }
     ctx_now = [len(s.token_ids) - 1 for s in seqs]
