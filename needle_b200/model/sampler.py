@@ -69,6 +69,35 @@ def filtered_logits(logits: torch.Tensor, temperature: Sequence[float], top_k: S
     return x
 
 
+def _step_params(owner, params_list, dev, generator):
+    """The step's per-row (temperature, top_k, top_p, uniform) device arrays.
+    An all-greedy step reuses arrays cached on ``owner`` (this library's
+    Sampler, or needle's once ``patch_needle()`` bound ``Sampler.sample`` to
+    it) and copies nothing; otherwise the parameters go over in one copy."""
+    n = len(params_list)
+    if all(p.temperature == 0.0 for p in params_list):
+        g = getattr(owner, "_nb_greedy", None)
+        if g is None or g[0].numel() < n or g[0].device != dev:
+            m = max(n, 256)
+            g = (torch.zeros(m, dtype=torch.float32, device=dev),
+                 torch.zeros(m, dtype=torch.int32, device=dev),
+                 torch.ones(m, dtype=torch.float32, device=dev),
+                 torch.zeros(m, dtype=torch.float32, device=dev))
+            owner._nb_greedy = g
+        return g
+    host = torch.empty(4 * n, dtype=torch.float32).pin_memory()
+    host[:n] = torch.tensor([float(p.temperature) for p in params_list])
+    host[n:2 * n].view(torch.int32)[:] = torch.tensor(
+        [int(p.top_k) if p.top_k > 0 else 0 for p in params_list], dtype=torch.int32)
+    host[2 * n:3 * n] = torch.tensor([float(p.top_p) for p in params_list])
+    d = host.to(dev, non_blocking=True)
+    if generator is not None and generator.device.type != "cuda":
+        u = torch.rand(n, generator=generator).to(dev, non_blocking=True)
+    else:
+        u = torch.rand(n, device=dev, generator=generator)
+    return d[:n], d[n:2 * n].view(torch.int32), d[2 * n:3 * n], u
+
+
 class Sampler:
     """Drop-in for needle's ``Sampler`` (same ``sample`` signature).
 
@@ -78,36 +107,6 @@ class Sampler:
     all-greedy step reuses cached parameter arrays and copies nothing).  CPU
     logits (host callers and tests) take the batched torch path below.
     """
-
-    def __init__(self):
-        self._greedy = None    # device arrays for all-greedy steps
-        self._stage = None     # pinned staging of per-row parameters
-
-    def _params(self, params_list, dev, generator):
-        from .. import ops  # noqa: F401  (the library must be loadable)
-        n = len(params_list)
-        if all(p.temperature == 0.0 for p in params_list):
-            # getattr: patch_needle() binds this method to needle's own Sampler
-            g = getattr(self, "_greedy", None)
-            if g is None or g[0].numel() < n or g[0].device != dev:
-                m = max(n, 256)
-                g = (torch.zeros(m, dtype=torch.float32, device=dev),
-                     torch.zeros(m, dtype=torch.int32, device=dev),
-                     torch.ones(m, dtype=torch.float32, device=dev),
-                     torch.zeros(m, dtype=torch.float32, device=dev))
-                self._greedy = g
-            return g
-        host = torch.empty(4 * n, dtype=torch.float32).pin_memory()
-        host[:n] = torch.tensor([float(p.temperature) for p in params_list])
-        host[n:2 * n].view(torch.int32)[:] = torch.tensor(
-            [int(p.top_k) if p.top_k > 0 else 0 for p in params_list], dtype=torch.int32)
-        host[2 * n:3 * n] = torch.tensor([float(p.top_p) for p in params_list])
-        d = host.to(dev, non_blocking=True)
-        if generator is not None and generator.device.type != "cuda":
-            u = torch.rand(n, generator=generator).to(dev, non_blocking=True)
-        else:
-            u = torch.rand(n, device=dev, generator=generator)
-        return d[:n], d[n:2 * n].view(torch.int32), d[2 * n:3 * n], u
 
     @torch.no_grad()
     def sample(self, logits: torch.Tensor, params_list: Sequence,
@@ -119,7 +118,7 @@ class Sampler:
         dev = logits.device
         if logits.is_cuda:
             from .. import ops
-            t, k, p, u = self._params(params_list, dev, generator)
+            t, k, p, u = _step_params(self, params_list, dev, generator)
             return ops.sample(logits, t, k, p, u).tolist()  # the step's only host read
         greedy = [p.temperature == 0.0 for p in params_list]
         ids = logits.argmax(dim=-1)
