@@ -70,7 +70,7 @@ def parse():
                     help="prefill workload: sequences x new tokens per sequence")
     ap.add_argument("--workload",
                     choices=["llama8b", "llama8b-c4", "qwen72b", "decode-op", "prefill",
-                             "allreduce", "store-kv", "kernel-cases"],
+                             "allreduce", "store-kv", "kernel-cases", "step-profile"],
                     default="llama8b",
                     help="llama8b (default): config 3, Llama-3-8B decode at batch 256, tp=N; "
                          "llama8b-c4: config 4 (512 requests, tp=N); qwen72b: config 5 (tp=N, "
@@ -1117,6 +1117,86 @@ def run_store_kv(args):
         dist.destroy_process_group()
 
 
+def run_step_profile(args):
+    """Where a config-3 decode step goes: the captured decode graph replayed
+    (as in ``value``) under torch.profiler, CUDA kernel time per step grouped
+    by kernel name, next to the CUDA-event time of the same replays without
+    the profiler.  One JSON line."""
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    from torch.profiler import ProfilerActivity, profile
+    from needle_b200 import ops
+    from needle_b200.model import ModelRunner, preset
+    from needle_b200.model.driver import BatchDriver, blocks_needed
+    from needle_b200.model.sequence import SamplingParams, SchedulerOutput
+    cfg = preset("llama3-8b")
+    prompts, _ = _model_prompts("llama8b", cfg)
+    runner = ModelRunner(cfg, block_size=16, dtype="bfloat16", device=str(dev))
+    runner.init_synthetic(seed=0)
+    nblk = blocks_needed([len(p) for p in prompts], 257, 16)
+    runner.init_kv_cache(nblk, 0)
+    drv = BatchDriver(runner, nblk)
+    seqs = [drv.add(p, SamplingParams(temperature=0.0, max_new_tokens=256)) for p in prompts]
+    drv.step()
+    longest = max(len(s.token_ids) for s in seqs)
+    runner.capture_decode_graphs(len(seqs), (longest + 64) // 16, (longest + 15) // 16)
+    for _ in range(max(3, args.warmup)):
+        drv.step()
+    for s in seqs:
+        tbl = drv.tables[s.seq_id]
+        while len(tbl) * 16 < len(s.token_ids) + 24:
+            tbl.append(drv.free.popleft())
+    inp = runner._prepare_inputs(SchedulerOutput(
+        prefill_seqs=[], decode_seqs=seqs, block_tables=drv.tables, swap_in_map={},
+        swap_out_map={}, blocks_to_free=[]))
+    B = len(seqs)
+    greedy = (torch.zeros(B, dtype=torch.float32, device=dev),
+              torch.zeros(B, dtype=torch.int32, device=dev),
+              torch.ones(B, dtype=torch.float32, device=dev),
+              torch.zeros(B, dtype=torch.float32, device=dev))
+
+    def step():
+        logits = runner._forward(inp)
+        ops.sample(logits, *greedy, out=inp.input_ids)
+        inp.position_ids.add_(1)
+        inp.context_lens.add_(1)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    n = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    step_ms = e0.elapsed_time(e1) / n
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            step()
+        torch.cuda.synchronize(dev)
+    agg = {}
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            a = agg.setdefault(ev.name, [0, 0.0])
+            a[0] += 1
+            a[1] += ev.device_time_total
+    tot = sum(v[1] for v in agg.values())
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+    print(json.dumps({
+        "metric": "config-3 decode step breakdown (us per step by kernel)",
+        "value": round(step_ms, 4), "unit": "ms/step", "n_gpus": 1, "steps": n, "warmup": 3,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "step-profile: config 3 decode graph replay"},
+        "kernel_us_per_step_total": round(tot / n, 1),
+        "kernels": [{"name": k[:160], "us_per_step": round(v[1] / n, 1),
+                     "launches_per_step": v[0] / n, "share": round(v[1] / tot, 4)}
+                    for k, v in rows[:24]],
+        "gpu_launches": None}), flush=True)
+    runner.close()
+
+
 def run_kernel_cases(args):
     """Per-kernel roofline figures for the kernels around the decode and
     prefill paths, each call timed alone with CUDA events on the launching
@@ -1210,6 +1290,18 @@ def run_kernel_cases(args):
          lambda: ops.swap_kv_blocks(gpu, cpu, pairs), bound="host link")
     del gpu, cpu
     torch.cuda.empty_cache()
+    # the dense projections of a config-3 decode step at M = 256 (cuBLAS
+    # through torch, as in the model): weight bytes / time
+    for name, (N_, K_) in (("qkv 6144x4096", (6144, 4096)), ("o_proj 4096x4096", (4096, 4096)),
+                           ("gate_up 28672x4096", (28672, 4096)),
+                           ("down 4096x14336", (4096, 14336)),
+                           ("lm_head 128256x4096", (128256, 4096))):
+        wgt = rnd(N_, K_)
+        xin = rnd(256, K_)
+        case(f"cuBLAS linear M=256 {name}", "cuBLAS (torch F.linear)", N_ * K_ * 2,
+             lambda: torch.nn.functional.linear(xin, wgt))
+        del wgt, xin
+    torch.cuda.empty_cache()
     # the batched sampler at the config 3 decode shape (256 x 128256 bf16):
     # greedy rows read the row once; sampled rows (top-k 50, top-p 0.9) make
     # several passes, all but the first from L2
@@ -1250,6 +1342,8 @@ def main():
         run_store_kv(args)
     elif args.workload == "kernel-cases":
         run_kernel_cases(args)
+    elif args.workload == "step-profile":
+        run_step_profile(args)
     elif args.workload in MODEL_WORKLOADS:
         run_model(args)
     else:
