@@ -454,24 +454,28 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const float inv = 1.f / l;
       T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)w.h * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        tmem_ld32(tO + lane_off + c * 32, v);
-        if (qi < len) {
+      // the whole O row in one batch of TMEM loads and one wait; O_X is
+      // handed back to the MMA warp before the conversion and the stores
+      uint32_t ov[D / 32][32];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) tmem_ld32_nowait(tO + lane_off + c * 32, ov[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
+      if (qi < len) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             uint32_t pk[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-              pk[e] = Mma<T>::pack(v[k * 8 + 2 * e] * inv, v[k * 8 + 2 * e + 1] * inv);
+              pk[e] = Mma<T>::pack(__uint_as_float(ov[c][k * 8 + 2 * e]) * inv,
+                                   __uint_as_float(ov[c][k * 8 + 2 * e + 1]) * inv);
             *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) =
                 make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-        }
       }
-      tc_fence_before();
-      mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
       ++nunits;
     }
     if (!ok) {
