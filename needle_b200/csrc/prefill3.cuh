@@ -83,6 +83,10 @@ __device__ __forceinline__ float exp2_poly(float x) {
 #ifndef NB_PF3_POLY
 #define NB_PF3_POLY 0
 #endif
+// threads per query row in the softmax groups (1 or 2)
+#ifndef NB_PF3_SPLIT_DEFAULT
+#define NB_PF3_SPLIT_DEFAULT 1
+#endif
 
 template <int D> struct Pf3Geom {
   static constexpr int kAtom = 128 * 128;       // 128 rows x 128 B
@@ -92,11 +96,30 @@ template <int D> struct Pf3Geom {
   static constexpr int kK = 2 * kTile;          // K ring: 2 stages
   static constexpr int kV = kK + 2 * kTile;     // V ring: 2 stages
   static constexpr int kBars = kV + 2 * kTile;
-  static constexpr int kSmem = kBars + 256 + 1024;
+  // row-max exchange [group][parity][half][row] and row-sum exchange
+  // [group][half][row] between the two warps that share a row (SPLIT = 2)
+  static constexpr int kXchg = kBars + 256;
+  static constexpr int kSmem = kXchg + (2 * 2 * 2 * 128 + 2 * 2 * 128) * 4 + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kSA = 0, kSB = 128, kOA = 256, kOB = 256 + D;
-  static constexpr int kThreads = 320;
 };
+template <int SPLIT> constexpr int pf3_threads() { return 64 + 256 * SPLIT; }
+
+// Named barrier of one softmax group (id 1 + group) that also ORs a
+// predicate over its threads: every thread of the group gets the same answer
+// (a group leaves its loops together, so no thread is left at a barrier).
+__device__ __forceinline__ bool group_bar_or(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 // Work unit u -> (query block, head, sequence); units with the most KV tiles
 // come first.  Units past a sequence's end are empty (every role skips them).
@@ -109,8 +132,11 @@ __device__ __forceinline__ Pf3Unit pf3_unit(int u, int hq, int B, int nqb) {
   return Pf3Unit{nqb - 1 - u / per, r % hq, r / hq};
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(320, 1)
+// SPLIT = 1: one softmax thread per query row (warps 2-9);
+// SPLIT = 2: two threads per row, one per half of the 128 scores (warps 2-17),
+// which halves the serial softmax work per tile.
+template <typename T, int D, int SPLIT>
+__global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
     prefill_tc3_kernel(const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
@@ -155,9 +181,9 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar_kfree + 8 * i, 1);
       mbar_init(bar_vfree + 8 * i, 1);
       mbar_init(bar_s + 8 * i, 1);
-      mbar_init(bar_p + 8 * i, 128);
+      mbar_init(bar_p + 8 * i, 128 * SPLIT);
       mbar_init(bar_o + 8 * i, 1);
-      mbar_init(bar_ofree + 8 * i, 128);
+      mbar_init(bar_ofree + 8 * i, 128 * SPLIT);
     }
     mbar_init(bar_qfree, 1);
     mbar_init(bar_end, 1);
@@ -338,15 +364,23 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ---------------- softmax groups + epilogue ----------------
-    const int x = (warp - 2) >> 2;  // 0 = tile A, 1 = tile B
+    constexpr int NC = 128 / SPLIT;        // score columns per thread
+    constexpr int NCC = NC / 32;           // 32-column TMEM chunks per thread
+    constexpr int OC = D / 32 / SPLIT;     // O chunks per thread
+    const int sw = warp - 2;
+    const int x = sw / (4 * SPLIT);        // 0 = tile A, 1 = tile B
+    const int hsel = (sw >> 2) % SPLIT;    // which half of the row (SPLIT = 2)
     // A warp reaches the TMEM lanes of its warp index mod 4: lanes [32 wq,
-    // 32 wq + 32).  Warps 2-5 (and 6-9) are quarters 2, 3, 0, 1: each group
-    // covers all 128 lanes, and a thread's query row is its TMEM lane.
+    // 32 wq + 32).  Each set of four warps is quarters 2, 3, 0, 1: it covers
+    // all 128 lanes, and a thread's query row is its TMEM lane.
     const int wq = warp & 3;
     const uint32_t tS = tmem + (x ? G::kSB : G::kSA);
-    const uint32_t tO = tmem + (x ? G::kOB : G::kOA);
+    const uint32_t tO = tmem + (x ? G::kOB : G::kOA) + hsel * (D / SPLIT);
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const int r = wq * 32 + lane;
+    float* xmax = reinterpret_cast<float*>(smem + G::kXchg);   // [2][2][2][128]
+    float* xsum = xmax + 2 * 2 * 2 * 128;                      // [2][2][128]
+    const int gbar = 1 + x, gthreads = 128 * SPLIT;
     uint32_t ns = 0, nunits = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
@@ -359,37 +393,53 @@ __global__ void __launch_bounds__(320, 1)
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_mine; ++j) {
         const bool got = mbar_wait_bounded(bar_s + 8 * x, ns & 1);
+        const int par = ns & 1;
         ++ns;
-        if (__any_sync(0xffffffffu, !got) || *abort_flag) {
+        if (SPLIT == 1 && (__any_sync(0xffffffffu, !got) || *abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sr[4][32];
+        uint32_t sr[NCC][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32_nowait(tS + lane_off + c * 32, sr[c]);
+        for (int c = 0; c < NCC; ++c)
+          tmem_ld32_nowait(tS + lane_off + hsel * NC + c * 32, sr[c]);
         tmem_wait_ld();
-        const int kb = j * 128;
+        const int kb = j * 128 + hsel * NC;  // key index of this thread's first column
         // whole tile below the diagonal and inside the sequence: no masking
-        const bool full = kb + 127 <= qi && kb + 128 <= len;
-        // row max over 8 independent accumulators (no 128-deep dependency)
+        const bool full = j * 128 + 127 <= qi && j * 128 + 128 <= len;
         float mxa[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mxa[a] = -INFINITY;
         if (!full) {
-          const int lim = min(qi, len - 1) - kb;  // last visible column of the row
+          const int lim = min(qi, len - 1) - kb;  // last visible column of this half
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < NCC; ++c)
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               if (c * 32 + i > lim) sr[c][i] = __float_as_uint(-INFINITY);
         }
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < NCC; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], __uint_as_float(sr[c][i]));
         float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
                          fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+        if constexpr (SPLIT == 2) {
+          // both halves of the row publish their maximum (double-buffered by
+          // tile parity); the barrier also tells the whole group whether any
+          // thread's wait gave up
+          xmax[((x * 2 + par) * 2 + hsel) * 128 + r] = mx;
+          // the barrier also orders this thread's completed S loads before
+          // the partner's P stores into the same TMEM columns
+          tc_fence_before();
+          if (group_bar_or(gbar, gthreads, !got || *abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          mx = fmaxf(mx, xmax[((x * 2 + par) * 2 + (hsel ^ 1)) * 128 + r]);
+        }
         mx *= scale_log2;  // scale > 0: max of scaled scores = scaled max
         const bool need = mx > m + kRescaleThreshold;
         float alpha = 1.f;
@@ -400,7 +450,7 @@ __global__ void __launch_bounds__(320, 1)
         const float neg_m = -m;
         float rsa[4] = {0.f, 0.f, 0.f, 0.f};  // row sum in 4 independent partials
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < NCC; ++c) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             uint32_t pk[8];
@@ -422,16 +472,17 @@ __global__ void __launch_bounds__(320, 1)
               rsa[e & 3] += p0 + p1;
               pk[e] = Mma<T>::pack(p0, p1);
             }
-            tmem_st8(tS + lane_off + c * 16 + hh * 8, pk);  // P over S's first 64 columns
+            // P over S's first 64 columns (this half's 32 / 64 of them)
+            tmem_st8(tS + lane_off + hsel * (NC / 2) + c * 16 + hh * 8, pk);
           }
         }
         const float rs = (rsa[0] + rsa[1]) + (rsa[2] + rsa[3]);
         if (j > 0 && __any_sync(0xffffffffu, need)) {
-          // rescale O_X (P_X(j-1).V_{j-1} is complete: the commit that
-          // signalled S_X(j) covers it; P_X(j).V_j waits for this group's
-          // arrival below)
+          // rescale this thread's O columns (P_X(j-1).V_{j-1} is complete:
+          // the commit that signalled S_X(j) covers it; P_X(j).V_j waits for
+          // this group's arrivals below)
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < OC; ++c) {
             float v[32];
             tmem_ld32(tO + lane_off + c * 32, v);
 #pragma unroll
@@ -440,31 +491,41 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         tmem_wait_st();
-        l = l * alpha + rs;
+        l = l * alpha + rs;  // this thread's share of the row sum
         tc_fence_before();
         mbar_arrive(bar_p + 8 * x);
       }
       if (!ok) break;
       // epilogue: O_X / l -> out rows
       const bool done = mbar_wait_bounded(bar_o + 8 * x, nunits & 1);
-      if (__any_sync(0xffffffffu, !done) || *abort_flag) {
-        ok = false;
-        break;
+      if constexpr (SPLIT == 1) {
+        if (__any_sync(0xffffffffu, !done) || *abort_flag) {
+          ok = false;
+          break;
+        }
+      } else {
+        xsum[(x * 2 + hsel) * 128 + r] = l;
+        if (group_bar_or(gbar, gthreads, !done || *abort_flag)) {
+          ok = false;
+          break;
+        }
+        // the same order of the two partial sums in both halves
+        l = xsum[(x * 2 + 0) * 128 + r] + xsum[(x * 2 + 1) * 128 + r];
       }
       tc_fence_after();
       const float inv = 1.f / l;
-      T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)w.h * D;
-      // the whole O row in one batch of TMEM loads and one wait; O_X is
-      // handed back to the MMA warp before the conversion and the stores
-      uint32_t ov[D / 32][32];
+      T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)w.h * D + hsel * (D / SPLIT);
+      // this thread's O columns in one batch of TMEM loads and one wait; O_X
+      // is handed back to the MMA warp before the conversion and the stores
+      uint32_t ov[OC][32];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) tmem_ld32_nowait(tO + lane_off + c * 32, ov[c]);
+      for (int c = 0; c < OC; ++c) tmem_ld32_nowait(tO + lane_off + c * 32, ov[c]);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
       if (qi < len) {
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c)
+        for (int c = 0; c < OC; ++c)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             uint32_t pk[4];
@@ -495,25 +556,45 @@ __global__ void __launch_bounds__(320, 1)
 
 namespace nbh {
 
-template <typename T, int D>
-int launch_prefill_tc3(const void* q, int64_t qs, const void* k, int64_t ks, const void* v,
-                       int64_t vs, int hq, int hk, int group, const int32_t* cu, int B, int T_,
-                       int max_seqlen, float sl2, void* out, int64_t os, int dtype,
-                       cudaStream_t st) {
+inline int pf3_split() {
+  static int v = [] {
+    const char* e = getenv("NB_PF3_SPLIT");  // "1" / "2": threads per query row (diagnostics)
+    return (e && e[0] == '1') ? 1 : (e && e[0] == '2') ? 2 : NB_PF3_SPLIT_DEFAULT;
+  }();
+  return v;
+}
+
+template <typename T, int D, int SPLIT>
+int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                         const int32_t* cu, int B, int hq, int group, int max_seqlen, float sl2,
+                         T* out, int64_t os, cudaStream_t st) {
   using G = nb::Pf3Geom<D>;
-  CUtensorMap qm, km, vm;
-  int rc = tensor_map_2d(&qm, q, dtype, (uint64_t)hq * D, T_, (uint64_t)qs * 2, 64, 128);
-  if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
-  if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
-  if (rc) return rc;
-  auto kern = nb::prefill_tc3_kernel<T, D>;
+  auto kern = nb::prefill_tc3_kernel<T, D, SPLIT>;
   if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc3")) return r2;
   const int nqb = (max_seqlen + 255) / 256;
   const int64_t units = (int64_t)nqb * hq * B;
   if (units > INT32_MAX) return fail(NB_ERR_UNSUPPORTED, "too many prefill work units");
   const int grid = (int)std::min<int64_t>(units, num_sms());
-  kern<<<grid, G::kThreads, G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, sl2, (T*)out, os);
+  kern<<<grid, nb::pf3_threads<SPLIT>(), G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, sl2,
+                                                          out, os);
   return check_launch("prefill_tc3");
+}
+
+template <typename T, int D>
+int launch_prefill_tc3(const void* q, int64_t qs, const void* k, int64_t ks, const void* v,
+                       int64_t vs, int hq, int hk, int group, const int32_t* cu, int B, int T_,
+                       int max_seqlen, float sl2, void* out, int64_t os, int dtype,
+                       cudaStream_t st) {
+  CUtensorMap qm, km, vm;
+  int rc = tensor_map_2d(&qm, q, dtype, (uint64_t)hq * D, T_, (uint64_t)qs * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
+  if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
+  if (rc) return rc;
+  if (pf3_split() == 2)
+    return launch_prefill_tc3_s<T, D, 2>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
+                                         os, st);
+  return launch_prefill_tc3_s<T, D, 1>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
+                                       os, st);
 }
 
 }  // namespace nbh
