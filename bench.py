@@ -1071,6 +1071,13 @@ def run_store_kv(args):
         t_store_r = timed(lambda i: ops.store_kvcache(ks[i], vs[i], cache, bts[i], ctx, cu))
         t_rope_r = timed(lambda i: ops.rope_store_kvcache(qs[i], ks[i], vs[i], cos, sin, cache,
                                                           bts[i], ctx, cu))
+        # a plain device copy of the same bytes (32 MiB read + 32 MiB written,
+        # rotating over the same four sets): what one launch of this size can
+        # reach, next to the kernel
+        srcs = [torch.cat([ks[i], vs[i]], dim=0) for i in range(NS)]
+        dsts = [torch.empty_like(srcs[i]) for i in range(NS)]
+        t_copy = timed(lambda i: dsts[i].copy_(srcs[i]))
+        del srcs, dsts
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         for i in range(K):
@@ -1084,6 +1091,7 @@ def run_store_kv(args):
     t_rope = max_over_ranks(t_rope, ws, dev)
     t_store_r = max_over_ranks(t_store_r, ws, dev)
     t_rope_r = max_over_ranks(t_rope_r, ws, dev)
+    t_copy = max_over_ranks(t_copy, ws, dev)
     peak, src = measured_hbm_peak()
     store_bytes = 2 * (2 * T * KV * D * 2)
     rope_bytes = 2 * T * H * D * 2 + 2 * T * KV * D * 2 + 2 * T * KV * D * 2 + 2 * T * D * 2
@@ -1107,6 +1115,9 @@ def run_store_kv(args):
                            "bytes_per_launch": rope_bytes, "GB/s": gb(rope_bytes, t_rope),
                            "frac": round(rope_bytes / (t_rope * 1e-3) / 1e9 / peak, 4)},
             "slot_mapping_ms": round(t_map, 5),
+            "same_size_copy": {"what": "torch copy_ of the same 32 MiB of K/V rows",
+                               "ms": round(t_copy, 5), "GB/s": gb(store_bytes, t_copy),
+                               "frac": round(store_bytes / (t_copy * 1e-3) / 1e9 / peak, 4)},
             "self_resolving": {"store_kvcache_ms": round(t_store_r, 5),
                                "store_GB/s": gb(store_bytes, t_store_r),
                                "rope_store_ms": round(t_rope_r, 5),
@@ -1256,16 +1267,21 @@ def run_kernel_cases(args):
         case(f"silu_mul {tag} x 14336", "silu_mul_kernel", 3 * T * inter * 2,
              lambda: ops.silu_mul(gu, out=o))
     del x, r, w, o, ro, gu
-    # paged decode: config 2 (tensor-core split + merge) and the SIMT kernel
-    # at GQA group 16 (32 query / 2 KV heads)
-    for kvh, tag, kern in ((8, "config 2 (group 4)", "paged_decode_tc_kernel + decode_merge_kernel"),
-                           (2, "group 16 (32/2 heads)", "paged_decode_simt_kernel + decode_merge_kernel")):
+    # paged decode: config 2 (tensor-core split + merge), GQA group 16 (32
+    # query / 2 KV heads: the tensor-core kernel in two 8-head chunks) and
+    # the SIMT kernel (fp32 cache, config-2 shape)
+    for kvh, tag, kern, dt in (
+            (8, "config 2 (group 4)", "paged_decode_tc_kernel + decode_merge_kernel", bf),
+            (2, "group 16 (32/2 heads)", "paged_decode_tc_kernel + decode_merge_kernel", bf),
+            (8, "fp32 config-2 shape (SIMT)", "paged_decode_simt_kernel + decode_merge_kernel",
+             torch.float32)):
         wl = decode_op_workload(batch=64, num_heads=32, num_kv_heads=kvh, head_dim=128,
-                                block_size=16, device=dev)
+                                block_size=16, dtype=dt, device=dev)
         B, maxb = wl["block_table"].shape
         plan = ops.DecodePlan(B, 32, kvh, 128, maxb, 16, dev)
         out = torch.empty_like(wl["q"])
-        case(f"paged_decode {tag}", kern, decode_alg_bytes(wl["seq_len"], kvh, 32, 128, 2),
+        case(f"paged_decode {tag}", kern,
+             decode_alg_bytes(wl["seq_len"], kvh, 32, 128, wl["q"].element_size()),
              lambda: ops.paged_decode(wl["q"], wl["kv_cache"], wl["block_table"],
                                       wl["context_lens"], wl["scale"], out=out, plan=plan))
         del wl, plan, out
@@ -1298,9 +1314,12 @@ def run_kernel_cases(args):
                            ("lm_head 128256x4096", (128256, 4096))):
         wgt = rnd(N_, K_)
         xin = rnd(256, K_)
+        yout = torch.empty(256, N_, dtype=bf, device=dev)
         case(f"cuBLAS linear M=256 {name}", "cuBLAS (torch F.linear)", N_ * K_ * 2,
              lambda: torch.nn.functional.linear(xin, wgt))
-        del wgt, xin
+        case(f"nb_linear M=256 {name}", "linear_tc_kernel", N_ * K_ * 2,
+             lambda: ops.linear(xin, wgt, out=yout))
+        del wgt, xin, yout
     torch.cuda.empty_cache()
     # the batched sampler at the config 3 decode shape (256 x 128256 bf16):
     # greedy rows read the row once; sampled rows (top-k 50, top-p 0.9) make

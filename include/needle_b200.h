@@ -342,6 +342,19 @@ NB_API int nb_sample(const void* logits, int64_t row_stride, int num_rows, int v
                      const float* uniforms, void* filtered, int64_t filtered_stride,
                      int64_t* token_ids, int dtype, void* stream);
 
+/*
+ * Dense projection of a decode step: y[M, N] = x[M, K] . weight[N, K]^T
+ * (+ bias[N] when bias is not NULL), fp32 accumulation, output rounded to
+ * the input dtype (bf16 or fp16).  Replaces the F.linear of needle's
+ * ColumnParallelLinear / RowParallelLinear (needle/layers/linear.py:44,
+ * :92) for batches of at most 256 rows; x and weight rows 16-byte aligned
+ * (K, x_stride and w_stride multiples of 8).  Returns NB_ERR_UNSUPPORTED
+ * for shapes outside that (the caller keeps its library GEMM).
+ */
+NB_API int nb_linear(const void* x, int64_t x_stride, const void* weight, int64_t w_stride,
+                     const void* bias, void* y, int64_t y_stride, int M, int N, int K, int dtype,
+                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

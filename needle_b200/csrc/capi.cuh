@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -50,6 +51,30 @@ int current_device() {
 }  // namespace
 
 namespace nbh {
+
+// Launch configuration with programmatic stream serialisation (programmatic
+// dependent launch): the grid may be scheduled while the previous kernel in
+// the stream drains; its kernels call griddep_wait() before reading anything.
+inline bool pdl_enabled() {
+  static int on = [] {
+    const char* e = getenv("NB_PDL");  // "0" launches without the attribute (diagnostics)
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
+}
+
+inline void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[1], dim3 grid,
+                       dim3 block, size_t smem, cudaStream_t st) {
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+}
+
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -147,7 +172,7 @@ int tensor_map_2d(CUtensorMap* out, const void* base, int dtype, uint64_t cols, 
 
 extern "C" {
 
-int nb_abi_version(void) { return 2; }
+int nb_abi_version(void) { return 3; }
 
 const char* nb_last_error(void) { return g_msg; }
 

@@ -474,29 +474,6 @@ __global__ void __launch_bounds__(128)
 // ---------------------------------------------------------------------------
 namespace nbh {
 
-// Launch configuration with programmatic stream serialisation (programmatic
-// dependent launch): the grid may be scheduled while the previous kernel in
-// the stream drains; its kernels call griddep_wait() before reading anything.
-inline bool pdl_enabled() {
-  static int on = [] {
-    const char* e = getenv("NB_PDL");  // "0" launches without the attribute (diagnostics)
-    return (e && e[0] == '0') ? 0 : 1;
-  }();
-  return on != 0;
-}
-
-inline void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[1], dim3 grid,
-                       dim3 block, size_t smem, cudaStream_t st) {
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-}
-
 // Tensor-core decode configuration: warps per CTA and TMA pipeline depth per
 // warp.  Each warp keeps one page id per lane, so a split holds at most
 // 32 * warps pages.

@@ -8,6 +8,7 @@
 #include "slots.cuh"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "linear.cuh"
 #include "norm.cuh"
 #include "act.cuh"
 #include "sample.cuh"

@@ -35,31 +35,6 @@
 
 namespace nb {
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane, without waiting
-// (pair with tmem_wait_ld).
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
-// Store 8 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // 2^x on the FMA/ALU pipes, for the share of the softmax exponentials that
 // would otherwise queue on the MUFU (XU) pipe, which limits this kernel.
 // Cody-Waite style range reduction: n = round(x) through the 1.5 * 2^23 magic
@@ -82,6 +57,10 @@ __device__ __forceinline__ float exp2_poly(float x) {
 // the MUFU in unmasked tiles.
 #ifndef NB_PF3_POLY
 #define NB_PF3_POLY 0
+#endif
+// 1: the epilogue reads all of O_X before handing it back; 0: chunk by chunk
+#ifndef NB_PF3_EPI_BATCH
+#define NB_PF3_EPI_BATCH 1
 #endif
 // threads per query row in the softmax groups (1 or 2)
 #ifndef NB_PF3_SPLIT_DEFAULT
@@ -515,6 +494,7 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       tc_fence_after();
       const float inv = 1.f / l;
       T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)w.h * D + hsel * (D / SPLIT);
+#if NB_PF3_EPI_BATCH
       // this thread's O columns in one batch of TMEM loads and one wait; O_X
       // is handed back to the MMA warp before the conversion and the stores
       uint32_t ov[OC][32];
@@ -537,6 +517,28 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
                 make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
       }
+#else
+      // one 32-column chunk at a time: load, convert, store; O_X handed back
+      // after the last chunk
+#pragma unroll 1
+      for (int c = 0; c < OC; ++c) {
+        float v[32];
+        tmem_ld32(tO + lane_off + c * 32, v);
+        if (qi < len) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pk[e] = Mma<T>::pack(v[k * 8 + 2 * e] * inv, v[k * 8 + 2 * e + 1] * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
+#endif
       ++nunits;
     }
     if (!ok) {

@@ -15,6 +15,8 @@
 // token-major K/V rows and of the 256-byte cache rows they land in).
 #pragma once
 #include <algorithm>
+#include <cstdlib>
+#include <type_traits>
 
 #include "nb_common.cuh"
 
@@ -79,6 +81,9 @@ __global__ void __launch_bounds__(256)
                                int64_t v_stride, T* __restrict__ cache, int num_blocks, int kvh,
                                int block_size, int D, const int32_t* __restrict__ slots,
                                int num_tokens) {
+  // launched with programmatic stream serialisation: the launch overlaps the
+  // previous kernel's tail, the reads wait for its results
+  griddep_wait();
   griddep_launch_dependents();  // the paged decode that follows may start its launch
   constexpr int VEC = 16 / sizeof(T);
   const int vpr = VPR ? VPR : D / VEC;
@@ -131,6 +136,7 @@ __global__ void __launch_bounds__(256)
                             int num_blocks, int hk, int block_size, int D,
                             const int32_t* __restrict__ slots, int num_tokens,
                             int write_k_back) {
+  griddep_wait();  // programmatic launch, as store_kvcache_slots_kernel
   griddep_launch_dependents();
   constexpr int VEC = 16 / sizeof(T);
   const int half = D / 2;
@@ -217,6 +223,16 @@ inline unsigned slot_grid(int64_t units) {
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+// 16-byte vectors per lane and unit of the slot writers: 4 or 8 (NB_KVW_U,
+// diagnostics).
+inline int kvw_unroll() {
+  static int v = [] {
+    const char* e = getenv("NB_KVW_U");
+    return (e && e[0] == '8') ? 8 : 4;
+  }();
+  return v;
+}
+
 template <typename T>
 int launch_store_slots(const void* k, int64_t ks, const void* v, int64_t vs, void* cache,
                        int nblk, int kvh, int bs, int D, const int32_t* slots, int ntok,
@@ -226,21 +242,25 @@ int launch_store_slots(const void* k, int64_t ks, const void* v, int64_t vs, voi
     return fail(NB_ERR_UNSUPPORTED,
                 "slot writers need 16-byte aligned rows (head_dim and strides multiples of %d)",
                 VEC);
-  constexpr int U = 4;
   const int per_tok = kvh * 2 * (D / VEC);
-  const int64_t units = (int64_t)ntok * ((per_tok + 32 * U - 1) / (32 * U));
-  if (units > INT32_MAX / 2) return fail(NB_ERR_UNSUPPORTED, "too many tokens for one launch");
-  const unsigned grid = slot_grid(units);
-  if (D / VEC == 16)
-    nb::store_kvcache_slots_kernel<T, 16, U><<<grid, 256, 0, st>>>(
-        (const T*)k, ks, (const T*)v, vs, (T*)cache, nblk, kvh, bs, D, slots, ntok);
-  else if (D / VEC == 8)
-    nb::store_kvcache_slots_kernel<T, 8, U><<<grid, 256, 0, st>>>(
-        (const T*)k, ks, (const T*)v, vs, (T*)cache, nblk, kvh, bs, D, slots, ntok);
-  else
-    nb::store_kvcache_slots_kernel<T, 0, U><<<grid, 256, 0, st>>>(
-        (const T*)k, ks, (const T*)v, vs, (T*)cache, nblk, kvh, bs, D, slots, ntok);
-  return check_launch("store_kvcache_slots");
+  auto go = [&](auto u_tag) -> int {
+    constexpr int U = decltype(u_tag)::value;
+    const int64_t units = (int64_t)ntok * ((per_tok + 32 * U - 1) / (32 * U));
+    if (units > INT32_MAX / 2) return fail(NB_ERR_UNSUPPORTED, "too many tokens for one launch");
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[1];
+    pdl_config(cfg, attr, dim3(slot_grid(units)), dim3(256), 0, st);
+    auto kern = D / VEC == 16  ? nb::store_kvcache_slots_kernel<T, 16, U>
+                : D / VEC == 8 ? nb::store_kvcache_slots_kernel<T, 8, U>
+                               : nb::store_kvcache_slots_kernel<T, 0, U>;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const T*)k, ks, (const T*)v, vs, (T*)cache,
+                                       nblk, kvh, bs, D, slots, ntok);
+    if (e != cudaSuccess)
+      return fail(NB_ERR_CUDA, "store_kvcache_slots launch: %s", cudaGetErrorString(e));
+    return check_launch("store_kvcache_slots");
+  };
+  if (kvw_unroll() == 8) return go(std::integral_constant<int, 8>());
+  return go(std::integral_constant<int, 4>());
 }
 
 template <typename T>
@@ -259,15 +279,17 @@ int launch_rope_store_slots(void* q, int64_t qs, int hq, void* k, int64_t ks, co
   const int per_tok = (hq + 2 * hk) * cpr;
   const int64_t units = (int64_t)ntok * ((per_tok + 32 * U - 1) / (32 * U));
   if (units > INT32_MAX / 2) return fail(NB_ERR_UNSUPPORTED, "too many tokens for one launch");
-  const unsigned grid = slot_grid(units);
-#define NB_RSS(C)                                                                              \
-  nb::rope_store_slots_kernel<T, C, U><<<grid, 256, 0, st>>>(                                 \
-      (T*)q, qs, hq, (T*)k, ks, (const T*)v, vs, (const T*)cos, (const T*)sin, css, (T*)cache, \
-      nblk, hk, bs, D, slots, ntok, wkb)
-  if (cpr == 8) NB_RSS(8);
-  else if (cpr == 4) NB_RSS(4);
-  else NB_RSS(0);
-#undef NB_RSS
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, dim3(slot_grid(units)), dim3(256), 0, st);
+  auto kern = cpr == 8   ? nb::rope_store_slots_kernel<T, 8, U>
+              : cpr == 4 ? nb::rope_store_slots_kernel<T, 4, U>
+                         : nb::rope_store_slots_kernel<T, 0, U>;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (T*)q, qs, hq, (T*)k, ks, (const T*)v, vs,
+                                     (const T*)cos, (const T*)sin, css, (T*)cache, nblk, hk, bs,
+                                     D, slots, ntok, wkb);
+  if (e != cudaSuccess)
+    return fail(NB_ERR_CUDA, "rope_store_kvcache_slots launch: %s", cudaGetErrorString(e));
   return check_launch("rope_store_kvcache_slots");
 }
 

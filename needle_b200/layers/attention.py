@@ -25,7 +25,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops
-from .linear import ColumnParallelLinear, RowParallelLinear
+from .linear import ColumnParallelLinear, RowParallelLinear, dense
 
 
 def _aligned16(*ts) -> bool:
@@ -90,7 +90,7 @@ class Attention(nn.Module):
         qkv_w = getattr(self, "_qkv_w", None)
         if qkv_w is not None:
             # one GEMM; q/k/v are column slices of its [T, (H + 2 KV) * D] output
-            qkv = F.linear(hidden_states, qkv_w, self._qkv_b)
+            qkv = dense(hidden_states, qkv_w, self._qkv_b)
             q = qkv[:, :H * D].view(T, H, D)
             k = qkv[:, H * D:(H + KV) * D].view(T, KV, D)
             v = qkv[:, (H + KV) * D:].view(T, KV, D)

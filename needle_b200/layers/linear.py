@@ -3,19 +3,42 @@
 Mirrors ``needle/layers/linear.py:21-98``: ``ColumnParallelLinear`` holds
 ``weight[out/tp, in]`` (+ optional bias) and needs no communication;
 ``RowParallelLinear`` holds ``weight[out, in/tp]`` and all-reduces (SUM) its
-output over the tensor-parallel group before adding the bias.  The GEMMs stay
-on torch (cuBLAS); the all-reduce is NCCL through ``torch.distributed``, or,
-with a ``TPComm`` attached, the fused all-reduce + residual + RMSNorm kernel
-run by the following ``RMSNorm``.
+output over the tensor-parallel group before adding the bias.  Every GEMM
+goes through ``dense``: decode-size batches (at most 256 rows, bf16 / fp16)
+on this library's tcgen05 kernel, everything else on torch (cuBLAS).  The
+all-reduce is NCCL through ``torch.distributed``, or, with a ``TPComm``
+attached, the fused all-reduce + residual + RMSNorm kernel run by the
+following ``RMSNorm``.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
 import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
+
+from .. import ops
+
+# "0": every GEMM stays on torch (diagnostics, A/B runs)
+_LINEAR_TC = os.environ.get("NB_LINEAR_TC", "1") != "0"
+
+
+def dense(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``F.linear(x, weight, bias)`` (into ``out`` when given): ``ops.linear``
+    for decode-size batches, torch otherwise."""
+    if _LINEAR_TC and ops.linear_supported(x, weight) and (
+            bias is None or (bias.dtype == x.dtype and bias.is_contiguous())):
+        return ops.linear(x, weight, bias, out=out)
+    if out is None:
+        return F.linear(x, weight, bias)
+    torch.mm(x, weight.t(), out=out)
+    if bias is not None:
+        out += bias
+    return out
 
 
 def tp_group():
@@ -41,7 +64,7 @@ class ColumnParallelLinear(nn.Module):
         nn.init.kaiming_uniform_(self.weight)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        out = F.linear(x, self.weight, self.bias)
+        out = dense(x, self.weight, self.bias)
         if self.gather_output and self.tp_size > 1:
             parts = [torch.empty_like(out) for _ in range(self.tp_size)]
             dist.all_gather(parts, out, group=tp_group())
@@ -68,8 +91,8 @@ class RowParallelLinear(nn.Module):
         if self.comm is not None and self.comm.can_fuse(x.shape[0]) and x.dim() == 2:
             # partial sums into the peer-mapped buffer; the following RMSNorm
             # all-reduces them together with the residual add and the norm
-            return torch.mm(x, self.weight.t(), out=self.comm.partial[:x.shape[0]])
-        out = F.linear(x, self.weight)
+            return dense(x, self.weight, out=self.comm.partial[:x.shape[0]])
+        out = dense(x, self.weight)
         if self.reduce_output and self.tp_size > 1:
             dist.all_reduce(out, op=dist.ReduceOp.SUM, group=tp_group())
         if self.bias is not None:

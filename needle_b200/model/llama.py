@@ -17,7 +17,7 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..layers.attention import Attention
-from ..layers.linear import ColumnParallelLinear, RowParallelLinear
+from ..layers.linear import ColumnParallelLinear, RowParallelLinear, dense
 from ..layers.norm import RMSNorm
 from ..layers.rope import RotaryEmbedding
 
@@ -44,7 +44,7 @@ class LlamaMLP(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self._gu_w is not None:
-            return self.down_proj(ops.silu_mul(F.linear(x, self._gu_w)))
+            return self.down_proj(ops.silu_mul(dense(x, self._gu_w)))
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -132,4 +132,4 @@ class LlamaForCausalLM(nn.Module):
                             context_lens, max_seqlen, is_prefill)
         if is_prefill:
             hidden = hidden[(cu_seqlens[1:] - 1).long()]
-        return self.lm_head(hidden)
+        return dense(hidden, self.lm_head.weight, self.lm_head.bias)

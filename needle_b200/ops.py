@@ -372,6 +372,41 @@ def silu_mul(gate_up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch
     return out
 
 
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x @ weight.T (+ bias)`` for a decode-size batch (at most 256 rows of
+    bf16 / fp16; rows of ``x`` and ``weight`` 16-byte aligned), on the
+    tcgen05 kernel ``nb_linear``.  ``out`` may be a row-strided view."""
+    _cuda(x, weight, bias, out)
+    if x.dim() != 2 or weight.dim() != 2 or x.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("linear: x [M, K] and weight [N, K] with unit column stride")
+    M, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K or weight.dtype != x.dtype:
+        raise ValueError(f"linear: weight {tuple(weight.shape)} {weight.dtype} does not match "
+                         f"x {tuple(x.shape)} {x.dtype}")
+    if bias is not None and (bias.shape != (N,) or bias.dtype != x.dtype or
+                             (N > 1 and bias.stride(0) != 1)):
+        raise ValueError("linear: bias must be a contiguous [N] tensor of x's dtype")
+    if out is None:
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    elif out.shape != (M, N) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise ValueError(f"linear: out must be [{M}, {N}] {x.dtype} with unit column stride")
+    L.check(L.lib().nb_linear(x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
+                              bias.data_ptr() if bias is not None else None, out.data_ptr(),
+                              out.stride(0), M, N, K, _dtype(x), _stream(x)))
+    return out
+
+
+def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether ``linear`` takes this GEMM (the shape checks of nb_linear)."""
+    return (x.is_cuda and x.dim() == 2 and 0 < x.shape[0] <= 256
+            and x.dtype in (torch.bfloat16, torch.float16) and weight.dtype == x.dtype
+            and weight.dim() == 2 and x.stride(1) == 1 and weight.stride(1) == 1
+            and x.shape[1] % 8 == 0 and x.stride(0) % 8 == 0 and weight.stride(0) % 8 == 0
+            and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0)
+
+
 def swap_kv_blocks(src_caches, dst_caches, pairs: torch.Tensor) -> None:
     """Copy blocks ``pairs[i, 0]`` of every layer's ``src_caches`` to blocks
     ``pairs[i, 1]`` of ``dst_caches`` (device <-> pinned host), one launch.

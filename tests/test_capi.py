@@ -17,7 +17,7 @@ def test_header_declares_the_hot_path():
                  "nb_last_error", "nb_device_errors", "nb_abi_version", "nb_silu_mul",
                  "nb_swap_kv_blocks", "nb_tp_allreduce_add_rmsnorm", "nb_ipc_handle",
                  "nb_ipc_open", "nb_ipc_close", "nb_paged_decode_noalloc",
-                 "nb_tp_set_wait_limit_ns"):
+                 "nb_tp_set_wait_limit_ns", "nb_linear", "nb_sample", "nb_slot_mapping"):
         assert name in decl, name
 
 
@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     for name in L.declared_functions():
         assert name in exported, f"{name} declared but not exported"
         assert getattr(lib, name) is not None
-    assert lib.nb_abi_version() == 2
+    assert lib.nb_abi_version() == 3
 
 
 def test_no_torch_types_in_signatures():
@@ -188,3 +188,19 @@ def test_swap_wrapper_rejects_mixed_layer_geometry():
         ops.swap_kv_blocks([a, b], [d, d], pairs)
     with pytest.raises(ValueError, match="every destination cache"):
         ops.swap_kv_blocks([a, a], [d, b], pairs)
+
+
+def test_linear_arg_checks():
+    lib = L.lib()
+    # more than 256 rows: not this kernel's shape (caller keeps its GEMM)
+    rc, msg = _err(lib.nb_linear(16, 64, 16, 64, None, 16, 64, 300, 64, 64, L.NB_DTYPE_BF16,
+                                 None))
+    assert rc == L.NB_ERR_UNSUPPORTED and "256" in msg
+    rc, msg = _err(lib.nb_linear(16, 64, 16, 64, None, 16, 64, 8, 64, 64, L.NB_DTYPE_F32, None))
+    assert rc == L.NB_ERR_UNSUPPORTED
+    # K not a multiple of 8 (TMA rows must be 16-byte aligned)
+    rc, msg = _err(lib.nb_linear(16, 68, 16, 68, None, 16, 64, 8, 64, 60, L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_UNSUPPORTED and "aligned" in msg
+    rc, msg = _err(lib.nb_linear(16, 32, 16, 64, None, 16, 64, 8, 64, 64, L.NB_DTYPE_BF16, None))
+    assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
+    assert lib.nb_linear(16, 64, 16, 64, None, 16, 64, 0, 64, 64, L.NB_DTYPE_BF16, None) == 0
