@@ -21,8 +21,18 @@
 //     the other partials to its own in rank order and writes its chunks of y
 //     (a fixed order: the result is the same on every run; one tile per
 //     cluster, S chosen by the host from the tile and SM counts);
-//   * S = 1: persistent CTAs over tiles with two accumulators, so the
-//     epilogue of one tile overlaps the MMAs of the next.
+//   * S = 1: persistent CTAs over tiles.  The default tile is 256 weight
+//     rows (two 128-row sub-tiles, two accumulators of all 512 TMEM columns)
+//     sharing each x tile: the weights are the only bytes that come from
+//     HBM, and at one CTA per SM the shared memory in flight (3 stages of
+//     64 KB) is what bounds a CTA's read rate, so the x share of every stage
+//     is kept to a half.  With 128-row tiles the two accumulator sets double-
+//     buffer instead, so the epilogue of one tile overlaps the next tile.
+//   The cluster split-K path (128-row tiles) is kept for shapes with few
+//   tiles, selected explicitly: a cluster of S CTAs must be co-resident, and
+//   the number of co-resident clusters (45 clusters of 3 at 197 KB of shared
+//   memory on a B200) caps it below one tile per cluster for the projections
+//   measured here; callers route those shapes to their library GEMM.
 //
 // Roles (192 threads): warp 0 TMA producer (one lane), warp 1 MMA issuer (one
 // lane), warps 2-5 epilogue (warp w reaches TMEM lanes 32 (w % 4) ..: the four
@@ -39,40 +49,47 @@
 
 namespace nb {
 
-constexpr int kLinStages = 4;
-constexpr int kLinW = 128 * 128;   // 128 weight rows x 64 K x 2 B
+constexpr int kLinW = 128 * 128;   // one 128-row weight sub-tile x 64 K x 2 B
 constexpr int kLinX = 256 * 128;   // up to 256 token rows x 64 K x 2 B
-constexpr int kLinStage = kLinW + kLinX;
-constexpr int kLinBars = kLinStages * kLinStage;  // 192 KB of stages
+// Pipeline depth: 4 stages of one sub-tile + x (48 KB), or 3 stages of two
+// sub-tiles + x (64 KB); 192 KB either way.
+template <int TW> constexpr int lin_stages() { return TW == 2 ? 3 : 4; }
+template <int TW> constexpr int lin_stage_bytes() { return TW * kLinW + kLinX; }
+constexpr int kLinBars = 192 * 1024;
 constexpr int kLinSmem = kLinBars + 256 + 1024;
 constexpr int kLinThreads = 192;
 constexpr int kLinChunk = 128 * 32 * 4;  // one 32-column chunk of a partial: 16 KB
 
-template <typename T, int S>
+// TW: 128-row weight sub-tiles per tile (1 or 2; a tile is 128 TW output
+// features).  S: CTAs per cluster splitting K (S > 1 only with TW = 1).
+template <typename T, int S, int TW>
 __global__ void __launch_bounds__(kLinThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                      const __grid_constant__ CUtensorMap xmap, T* __restrict__ y, int64_t ldy,
                      const T* __restrict__ bias, int M, int N, int NT, int n_tiles, int KB) {
+  static_assert(S == 1 || TW == 1, "the cluster split takes one sub-tile per tile");
   constexpr bool kBf16 = !__is_same(T, __half);
+  constexpr int kStages = lin_stages<TW>();
+  constexpr int kStage = lin_stage_bytes<TW>();
+  // accumulator sets: two (double buffering) when a tile's accumulators fit
+  // twice in tensor memory, else one
+  constexpr int kNbuf = (S == 1 && TW == 1) ? 2 : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // programmatic launch: the next kernel may be scheduled once every CTA of
-  // this one runs; it waits for this grid's completion before its reads
-  griddep_launch_dependents();
   const uint32_t sb = smem_u32(smem);
   const uint32_t bar_full = sb + kLinBars;        // [4] stage landed
   const uint32_t bar_empty = bar_full + 32;       // [4] stage read by its MMAs
-  const uint32_t bar_acc = bar_full + 64;         // [2] accumulator final
-  const uint32_t bar_accfree = bar_full + 80;     // [2] accumulator read out (128 arrivals)
+  const uint32_t bar_acc = bar_full + 64;         // [2] accumulator set final
+  const uint32_t bar_accfree = bar_full + 80;     // [2] accumulator set read out (128 arrivals)
   const uint32_t bar_ready = bar_full + 96;       // S > 1: the other CTAs' stages are free
   const uint32_t bar_recv = bar_full + 104;       // S > 1: the other CTAs' chunks landed here
   const uint32_t bar_end = bar_full + 112;        // every MMA of this CTA finished
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kLinBars + 128);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kLinBars + 136);
-  const uint32_t buf_cols = NT <= 128 ? 128u : 256u;
-  const uint32_t tmem_cols = S == 1 ? 2 * buf_cols : buf_cols;
+  const uint32_t acc_cols = NT <= 128 ? 128u : 256u;  // one sub-tile's accumulator
+  const uint32_t tmem_cols = kNbuf * TW * acc_cols;   // <= 512
   const int rank = S == 1 ? 0 : (int)cluster_ctarank();
 
   if (warp == 1) {
@@ -82,7 +99,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&wmap);
     prefetch_tensormap(&xmap);
-    for (int i = 0; i < kLinStages; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(bar_full + 8 * i, 1);
       mbar_init(bar_empty + 8 * i, 1);
     }
@@ -109,43 +126,47 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      const uint32_t bytes = kLinW + (uint32_t)NT * 128;
+      const uint32_t bytes = TW * kLinW + (uint32_t)NT * 128;
       const int kper = kb1 - kb0;
       const int n_mine = tile0 < n_tiles ? ((n_tiles - 1 - tile0) / tstep + 1) * kper : 0;
+      auto load_w = [&](uint32_t dst, int t, int kb, uint32_t bar) {
+#pragma unroll
+        for (int w = 0; w < TW; ++w)
+          tma_load_2d(dst + w * kLinW, &wmap, kb * 64, (t * TW + w) * 128, bar);
+      };
       // The weights do not depend on the previous kernel: the first stages'
       // weight tiles are requested before the programmatic-launch wait, the
       // activation tiles after it.
-      const int pre = n_mine < kLinStages ? n_mine : kLinStages;
+      const int pre = n_mine < kStages ? n_mine : kStages;
       for (int j = 0; j < pre; ++j) {
-        const int t = tile0 + (j / kper) * tstep, kb = kb0 + j % kper;
         mbar_arrive_expect_tx(bar_full + 8 * j, bytes);
-        tma_load_2d(sb + j * kLinStage, &wmap, kb * 64, t * 128, bar_full + 8 * j);
+        load_w(sb + j * kStage, tile0 + (j / kper) * tstep, kb0 + j % kper, bar_full + 8 * j);
       }
       griddep_wait();
       for (int j = 0; j < pre; ++j)
-        tma_load_2d(sb + j * kLinStage + kLinW, &xmap, (kb0 + j % kper) * 64, 0,
+        tma_load_2d(sb + j * kStage + TW * kLinW, &xmap, (kb0 + j % kper) * 64, 0,
                     bar_full + 8 * j);
       uint32_t it = (uint32_t)pre;
       bool ok = true;
       for (int j = pre; ok && j < n_mine; ++j, ++it) {
         const int t = tile0 + (j / kper) * tstep, kb = kb0 + j % kper;
-        const uint32_t st = it % kLinStages, round = it / kLinStages;
+        const uint32_t st = it % kStages, round = it / kStages;
         if (*abort_flag || !mbar_wait_bounded(bar_empty + 8 * st, (round & 1) ^ 1)) {
           ok = false;
           break;
         }
-        const uint32_t dst = sb + st * kLinStage;
+        const uint32_t dst = sb + st * kStage;
         mbar_arrive_expect_tx(bar_full + 8 * st, bytes);
-        tma_load_2d(dst, &wmap, kb * 64, t * 128, bar_full + 8 * st);
-        tma_load_2d(dst + kLinW, &xmap, kb * 64, 0, bar_full + 8 * st);
+        load_w(dst, t, kb, bar_full + 8 * st);
+        tma_load_2d(dst + TW * kLinW, &xmap, kb * 64, 0, bar_full + 8 * st);
       }
       if (!ok) {
         *abort_flag = 1;
         set_error(kErrTimeout);
       }
       // copies still in flight land before the CTA moves on
-      for (uint32_t j = it > kLinStages ? it - kLinStages : 0; j < it; ++j)
-        mbar_wait_bounded(bar_full + 8 * (j % kLinStages), (j / kLinStages) & 1);
+      for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0; j < it; ++j)
+        mbar_wait_bounded(bar_full + 8 * (j % kStages), (j / kStages) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -156,27 +177,29 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       int i = 0;
       bool ok = true;
       for (int t = tile0; ok && t < n_tiles; t += tstep, ++i) {
-        const int buf = S == 1 ? (i & 1) : 0;
-        if (S == 1 && i >= 2 &&
-            (*abort_flag || !mbar_wait_bounded(bar_accfree + 8 * buf, ((i >> 1) & 1) ^ 1))) {
+        const int buf = i % kNbuf, use = i / kNbuf;
+        if (use > 0 &&
+            (*abort_flag || !mbar_wait_bounded(bar_accfree + 8 * buf, (use & 1) ^ 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + buf * buf_cols;
+        const uint32_t d = tmem + buf * TW * acc_cols;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const uint32_t st = it % kLinStages, round = it / kLinStages;
+          const uint32_t st = it % kStages, round = it / kStages;
           if (*abort_flag || !mbar_wait_bounded(bar_full + 8 * st, round & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a = sb + st * kLinStage, b = a + kLinW;
+          const uint32_t a = sb + st * kStage, b = a + TW * kLinW;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma_f16_ss(d, smem_desc_sw128(a + kk * 32, 16, 1024),
-                          smem_desc_sw128(b + kk * 32, 16, 1024), idesc,
-                          (kb > kb0 || kk > 0) ? 1u : 0u);
+          for (int w = 0; w < TW; ++w)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_f16_ss(d + w * acc_cols, smem_desc_sw128(a + w * kLinW + kk * 32, 16, 1024),
+                            smem_desc_sw128(b + kk * 32, 16, 1024), idesc,
+                            (kb > kb0 || kk > 0) ? 1u : 0u);
           tc_commit(bar_empty + 8 * st);  // the stage may be refilled
         }
         if (!ok) break;
@@ -193,7 +216,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     // ---------------- epilogue ----------------
     griddep_wait();
     const int q = warp & 3;
-    const int nl = q * 32 + lane;  // this thread's output feature within the tile
+    const int nl = q * 32 + lane;  // this thread's output feature within a sub-tile
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const int nchunks = NT / 32;
     auto store_chunk = [&](int n, int c, const float (&v)[32]) {
@@ -208,28 +231,32 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     if constexpr (S == 1) {
       int i = 0;
       for (int t = tile0; t < n_tiles; t += tstep, ++i) {
-        const int buf = i & 1;
+        const int buf = i % kNbuf, use = i / kNbuf;
         // warp-uniform decision: the TMEM loads below are .sync.aligned
-        const bool bad = !mbar_wait_bounded(bar_acc + 8 * buf, (i >> 1) & 1) || *abort_flag;
+        const bool bad = !mbar_wait_bounded(bar_acc + 8 * buf, use & 1) || *abort_flag;
         if (__any_sync(0xffffffffu, bad)) {
           *abort_flag = 1;
           if (lane == 0) set_error(kErrTimeout);
           break;
         }
         tc_fence_after();
-        const int n = t * 128 + nl;
-        for (int c = 0; c < nchunks; ++c) {
-          uint32_t r[32];
-          tmem_ld32_nowait(tmem + buf * buf_cols + lane_off + c * 32, r);
-          tmem_wait_ld();
-          float v[32];
+#pragma unroll 1
+        for (int w = 0; w < TW; ++w) {
+          const int n = (t * TW + w) * 128 + nl;
+          const uint32_t base = tmem + (buf * TW + w) * acc_cols + lane_off;
+          for (int c = 0; c < nchunks; ++c) {
+            uint32_t r[32];
+            tmem_ld32_nowait(base + c * 32, r);
+            tmem_wait_ld();
+            float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (c + 1 == nchunks) {
-            tc_fence_before();
-            mbar_arrive(bar_accfree + 8 * buf);  // the MMA warp may reuse the accumulator
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (w + 1 == TW && c + 1 == nchunks) {
+              tc_fence_before();
+              mbar_arrive(bar_accfree + 8 * buf);  // the MMA warp may reuse the set
+            }
+            store_chunk(n, c, v);
           }
-          store_chunk(n, c, v);
         }
       }
     } else {
@@ -293,6 +320,9 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       }
     }
   }
+  // programmatic launch: the next kernel may be scheduled now; it waits for
+  // this grid's completion before reading anything
+  griddep_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (S > 1) cluster_sync_all();  // no CTA leaves while another may still write to it
@@ -306,30 +336,26 @@ __global__ void __launch_bounds__(kLinThreads, 1)
 
 namespace nbh {
 
-// Cluster size for n_tiles tiles of KB k-blocks: the smallest estimated time
-// (waves x k-blocks per CTA, plus a fixed reduction cost in k-block units).
-inline int linear_split(int n_tiles, int KB) {
-  const char* e = getenv("NB_LINEAR_SPLIT");  // diagnostics: force 1..4
-  if (e && e[0] >= '1' && e[0] <= '4') return std::min(e[0] - '0', std::max(1, KB));
-  const int sms = num_sms();
-  double best = (double)((n_tiles + sms - 1) / sms) * KB;
-  int bs = 1;
-  for (int s = 2; s <= 4 && s <= KB; ++s) {
-    const int per_wave = std::max(1, sms / s);
-    const double t = (double)((n_tiles + per_wave - 1) / per_wave) * ((KB + s - 1) / s + 3);
-    if (t < 0.95 * best) {
-      best = t;
-      bs = s;
-    }
-  }
-  return bs;
+// Shape of the launch: TW (128-row weight sub-tiles per tile) and S (CTAs
+// per cluster splitting K).  Default: 256-row tiles (TW = 2) on persistent
+// CTAs, the most weight bytes in flight per SM.  NB_LINEAR_SPLIT=2..4 takes
+// the cluster split-K path with 128-row tiles, NB_LINEAR_SPLIT=1 128-row
+// tiles without a split (diagnostics and tests).
+struct LinPlan {
+  int tw, s;
+};
+inline LinPlan linear_plan(int KB) {
+  const char* e = getenv("NB_LINEAR_SPLIT");
+  if (e && e[0] >= '1' && e[0] <= '4') return LinPlan{1, std::min(e[0] - '0', std::max(1, KB))};
+  return LinPlan{2, 1};
 }
 
-template <typename T, int S>
+template <typename T, int S, int TW>
 int launch_linear_s(const CUtensorMap& wm, const CUtensorMap& xm, void* y, int64_t ldy,
-                    const void* bias, int M, int N, int NT, int n_tiles, int KB, cudaStream_t st) {
-  auto kern = nb::linear_tc_kernel<T, S>;
+                    const void* bias, int M, int N, int NT, int KB, cudaStream_t st) {
+  auto kern = nb::linear_tc_kernel<T, S, TW>;
   if (int r = ensure_max_smem((const void*)kern, nb::kLinSmem, "linear_tc")) return r;
+  const int n_tiles = (N + 128 * TW - 1) / (128 * TW);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   cfg.blockDim = dim3(nb::kLinThreads);
@@ -360,17 +386,18 @@ template <typename T>
 int launch_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
                   void* y, int64_t ldy, int M, int N, int K, int dtype, cudaStream_t st) {
   const int NT = (M + 31) / 32 * 32;
-  const int n_tiles = (N + 127) / 128;
   const int KB = (K + 63) / 64;
   CUtensorMap wm, xm;
   int rc = tensor_map_2d(&wm, w, dtype, (uint64_t)K, (uint64_t)N, (uint64_t)ldw * 2, 64, 128);
   if (!rc) rc = tensor_map_2d(&xm, x, dtype, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, 64, NT);
   if (rc) return rc;
-  switch (linear_split(n_tiles, KB)) {
-    case 2: return launch_linear_s<T, 2>(wm, xm, y, ldy, bias, M, N, NT, n_tiles, KB, st);
-    case 3: return launch_linear_s<T, 3>(wm, xm, y, ldy, bias, M, N, NT, n_tiles, KB, st);
-    case 4: return launch_linear_s<T, 4>(wm, xm, y, ldy, bias, M, N, NT, n_tiles, KB, st);
-    default: return launch_linear_s<T, 1>(wm, xm, y, ldy, bias, M, N, NT, n_tiles, KB, st);
+  const LinPlan p = linear_plan(KB);
+  if (p.tw == 2) return launch_linear_s<T, 1, 2>(wm, xm, y, ldy, bias, M, N, NT, KB, st);
+  switch (p.s) {
+    case 2: return launch_linear_s<T, 2, 1>(wm, xm, y, ldy, bias, M, N, NT, KB, st);
+    case 3: return launch_linear_s<T, 3, 1>(wm, xm, y, ldy, bias, M, N, NT, KB, st);
+    case 4: return launch_linear_s<T, 4, 1>(wm, xm, y, ldy, bias, M, N, NT, KB, st);
+    default: return launch_linear_s<T, 1, 1>(wm, xm, y, ldy, bias, M, N, NT, KB, st);
   }
 }
 

@@ -100,15 +100,37 @@ __device__ __forceinline__ bool group_bar_or(int id, int nthreads, bool pred) {
   return r != 0;
 }
 
+// max(a, b, c) in one instruction (sm_100 three-input max; NaN handling as
+// fmaxf: a NaN operand is ignored).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Work unit u -> (query block, head, sequence); units with the most KV tiles
 // come first.  Units past a sequence's end are empty (every role skips them).
+// Two ways to give the two softmax groups their 128-row query tiles:
+//   pair = 0: the two halves of a 256-row block of one head (tile B sees one
+//             KV tile more than tile A);
+//   pair = 1: one 128-row block of two heads that share a KV head (even GQA
+//             groups): both tiles see the same KV tiles, so the groups stay
+//             in step to the unit's end and every K/V tile serves both.
 struct Pf3Unit {
-  int qb, h, b;
+  int qb, h, b;  // h: the head of tile A (pair = 1: tile B is head h + 1)
 };
-__device__ __forceinline__ Pf3Unit pf3_unit(int u, int hq, int B, int nqb) {
-  const int per = hq * B;
+__device__ __forceinline__ Pf3Unit pf3_unit(int u, int hq, int B, int nqb, int pair) {
+  const int hu = pair ? hq / 2 : hq;
+  const int per = hu * B;
   const int r = u % per;
-  return Pf3Unit{nqb - 1 - u / per, r % hq, r / hq};
+  return Pf3Unit{nqb - 1 - u / per, (r % hu) * (pair ? 2 : 1), r / hu};
+}
+// First query row (within the sequence) and head of tile x of a unit.
+__device__ __forceinline__ int pf3_row(const Pf3Unit& w, int x, int pair) {
+  return pair ? w.qb * 128 : w.qb * 256 + x * 128;
+}
+__device__ __forceinline__ int pf3_head(const Pf3Unit& w, int x, int pair) {
+  return pair ? w.h + x : w.h;
 }
 
 // SPLIT = 1: one softmax thread per query row (warps 2-9);
@@ -119,8 +141,8 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
     prefill_tc3_kernel(const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
-                       int B, int hq, int group, int nqb, float scale_log2, T* __restrict__ out,
-                       int64_t os) {
+                       int B, int hq, int group, int nqb, int pair, float scale_log2,
+                       T* __restrict__ out, int64_t os) {
   using G = Pf3Geom<D>;
   constexpr bool kBf16 = !__is_same(T, __half);
   constexpr uint32_t kIdS = idesc_f16_f32(kBf16, 128, 128, false, false);
@@ -173,16 +195,20 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_units = nqb * hq * B;
+  const int n_units = nqb * (pair ? hq / 2 : hq) * B;
 
   // Causal extent of a unit: KV tiles under tile A / tile B (0: no tile B).
   auto extent = [&](const Pf3Unit& w, int& s0, int& len, int& nA, int& nB) -> bool {
     s0 = __ldg(cu + w.b);
     len = __ldg(cu + w.b + 1) - s0;
-    const int q0 = w.qb * 256;
+    const int q0 = pf3_row(w, 0, pair);
     if (q0 >= len) return false;
-    nA = 2 * w.qb + 1;
-    nB = q0 + 128 < len ? 2 * w.qb + 2 : 0;
+    if (pair) {
+      nA = nB = w.qb + 1;
+    } else {
+      nA = 2 * w.qb + 1;
+      nB = q0 + 128 < len ? 2 * w.qb + 2 : 0;
+    }
     return true;
   };
 
@@ -192,19 +218,20 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       uint32_t nq = 0, nk = 0, nv = 0;  // loads issued (running counts)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-        const Pf3Unit w = pf3_unit(u, hq, B, nqb);
+        const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
         int s0, len, nA, nB;
         if (!extent(w, s0, len, nA, nB)) continue;
-        const int kh = w.h / group, q0 = w.qb * 256;
+        const int kh = w.h / group;
         const int n_kv = nB ? nB : nA;
         if (nq > 0 && !mbar_wait_bounded(bar_qfree, (nq - 1) & 1)) { ok = false; break; }
         mbar_arrive_expect_tx(bar_q, (nB ? 2 : 1) * G::kTile);
 #pragma unroll
         for (int a = 0; a < D / 64; ++a) {
-          tma_load_2d(sb + G::kQA + a * G::kAtom, &qmap, w.h * D + a * 64, s0 + q0, bar_q);
+          tma_load_2d(sb + G::kQA + a * G::kAtom, &qmap, pf3_head(w, 0, pair) * D + a * 64,
+                      s0 + pf3_row(w, 0, pair), bar_q);
           if (nB)
-            tma_load_2d(sb + G::kQB + a * G::kAtom, &qmap, w.h * D + a * 64, s0 + q0 + 128,
-                        bar_q);
+            tma_load_2d(sb + G::kQB + a * G::kAtom, &qmap, pf3_head(w, 1, pair) * D + a * 64,
+                        s0 + pf3_row(w, 1, pair), bar_q);
         }
         ++nq;
         for (int j = 0; j < n_kv; ++j) {
@@ -271,7 +298,7 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
                         (!first || kk > 0) ? 1u : 0u);
       };
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-        const Pf3Unit w = pf3_unit(u, hq, B, nqb);
+        const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
         int s0, len, nA, nB;
         if (!extent(w, s0, len, nA, nB)) continue;
         const int n_kv = nB ? nB : nA;
@@ -363,12 +390,12 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
     uint32_t ns = 0, nunits = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-      const Pf3Unit w = pf3_unit(u, hq, B, nqb);
+      const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
       int s0, len, nA, nB;
       if (!extent(w, s0, len, nA, nB)) continue;
       const int n_mine = x ? nB : nA;
       if (n_mine == 0) continue;
-      const int qi = w.qb * 256 + x * 128 + r;
+      const int qi = pf3_row(w, x, pair) + r;
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_mine; ++j) {
         const bool got = mbar_wait_bounded(bar_s + 8 * x, ns & 1);
@@ -401,9 +428,11 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
 #pragma unroll
         for (int c = 0; c < NCC; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], __uint_as_float(sr[c][i]));
-        float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                         fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+          for (int i = 0; i < 32; i += 2)
+            mxa[(i >> 1) & 7] = fmax3(mxa[(i >> 1) & 7], __uint_as_float(sr[c][i]),
+                                      __uint_as_float(sr[c][i + 1]));
+        float mx = fmax3(fmax3(mxa[0], mxa[1], mxa[2]), fmax3(mxa[3], mxa[4], mxa[5]),
+                         fmaxf(mxa[6], mxa[7]));
         if constexpr (SPLIT == 2) {
           // both halves of the row publish their maximum (double-buffered by
           // tile parity); the barrier also tells the whole group whether any
@@ -493,7 +522,8 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       }
       tc_fence_after();
       const float inv = 1.f / l;
-      T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)w.h * D + hsel * (D / SPLIT);
+      T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)pf3_head(w, x, pair) * D +
+               hsel * (D / SPLIT);
 #if NB_PF3_EPI_BATCH
       // this thread's O columns in one batch of TMEM loads and one wait; O_X
       // is handed back to the MMA warp before the conversion and the stores
@@ -566,6 +596,16 @@ inline int pf3_split() {
   return v;
 }
 
+// Head pairs for even GQA groups (NB_PF3_PAIR=0 keeps the row halves of one
+// head; diagnostics).
+inline int pf3_pair_heads(int group) {
+  static int on = [] {
+    const char* e = getenv("NB_PF3_PAIR");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return (on && group % 2 == 0) ? 1 : 0;
+}
+
 template <typename T, int D, int SPLIT>
 int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                          const int32_t* cu, int B, int hq, int group, int max_seqlen, float sl2,
@@ -573,12 +613,13 @@ int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUt
   using G = nb::Pf3Geom<D>;
   auto kern = nb::prefill_tc3_kernel<T, D, SPLIT>;
   if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc3")) return r2;
-  const int nqb = (max_seqlen + 255) / 256;
-  const int64_t units = (int64_t)nqb * hq * B;
+  const int pair = pf3_pair_heads(group);
+  const int nqb = pair ? (max_seqlen + 127) / 128 : (max_seqlen + 255) / 256;
+  const int64_t units = (int64_t)nqb * (pair ? hq / 2 : hq) * B;
   if (units > INT32_MAX) return fail(NB_ERR_UNSUPPORTED, "too many prefill work units");
   const int grid = (int)std::min<int64_t>(units, num_sms());
-  kern<<<grid, nb::pf3_threads<SPLIT>(), G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, sl2,
-                                                          out, os);
+  kern<<<grid, nb::pf3_threads<SPLIT>(), G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, pair,
+                                                          sl2, out, os);
   return check_launch("prefill_tc3");
 }
 

@@ -5,7 +5,8 @@ Mirrors ``needle/layers/linear.py:21-98``: ``ColumnParallelLinear`` holds
 ``RowParallelLinear`` holds ``weight[out, in/tp]`` and all-reduces (SUM) its
 output over the tensor-parallel group before adding the bias.  Every GEMM
 goes through ``dense``: decode-size batches (at most 256 rows, bf16 / fp16)
-on this library's tcgen05 kernel, everything else on torch (cuBLAS).  The
+with many output features (the gate/up projection, the LM head) on this
+library's tcgen05 kernel, everything else on torch (cuBLAS).  The
 all-reduce is NCCL through ``torch.distributed``, or, with a ``TPComm``
 attached, the fused all-reduce + residual + RMSNorm kernel run by the
 following ``RMSNorm``.
@@ -29,8 +30,9 @@ _LINEAR_TC = os.environ.get("NB_LINEAR_TC", "1") != "0"
 def dense(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
           out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``F.linear(x, weight, bias)`` (into ``out`` when given): ``ops.linear``
-    for decode-size batches, torch otherwise."""
-    if _LINEAR_TC and ops.linear_supported(x, weight) and (
+    for decode-size batches where it beats the library GEMM
+    (``ops.linear_preferred``), torch otherwise."""
+    if _LINEAR_TC and ops.linear_preferred(x, weight) and (
             bias is None or (bias.dtype == x.dtype and bias.is_contiguous())):
         return ops.linear(x, weight, bias, out=out)
     if out is None:

@@ -407,6 +407,22 @@ def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
             and x.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0)
 
 
+_SMS = {}
+
+
+def linear_preferred(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether ``linear`` is the faster choice for this GEMM on this GPU:
+    supported, and enough 256-row weight tiles (``N / 256``) to keep at
+    least 65 % of the SMs streaming weights.  Projections with fewer tiles
+    (Llama-3-8B qkv, o_proj, down at one GPU) measure faster on cuBLAS."""
+    if not linear_supported(x, weight):
+        return False
+    dev = x.device.index
+    if dev not in _SMS:
+        _SMS[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
+    return (weight.shape[0] + 255) // 256 >= 0.65 * _SMS[dev]
+
+
 def swap_kv_blocks(src_caches, dst_caches, pairs: torch.Tensor) -> None:
     """Copy blocks ``pairs[i, 0]`` of every layer's ``src_caches`` to blocks
     ``pairs[i, 1]`` of ``dst_caches`` (device <-> pinned host), one launch.

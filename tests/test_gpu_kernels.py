@@ -424,17 +424,21 @@ print('ok')
 """
 
 
-@pytest.mark.parametrize("version", ["1", "2", "3"])
+@pytest.mark.parametrize("version", ["1", "2", "3", "3-rows"])
 def test_prefill_every_kernel_version(cuda, version):
     """Every tensor-core prefill kernel (single softmax group / two ping-pong
-    groups per CTA / persistent warp-specialised), selected through
-    NB_PREFILL_V in a fresh process, on lengths around the 128- and 256-row
-    tile edges, bf16 and fp16."""
+    groups per CTA / persistent warp-specialised, the last with head-pair
+    units for even GQA groups and, "3-rows", with the row halves of one head
+    for every group), selected through NB_PREFILL_V / NB_PF3_PAIR in a fresh
+    process, on lengths around the 128- and 256-row tile edges, bf16 and
+    fp16."""
     import os
     import subprocess
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, NB_PREFILL_V=version)
+    env = dict(os.environ, NB_PREFILL_V=version[0])
+    if version == "3-rows":
+        env["NB_PF3_PAIR"] = "0"
     r = subprocess.run([sys.executable, "-c", _PREFILL_CHECK], cwd=root, env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]

@@ -1,16 +1,14 @@
-"""The decode-step projection ``nb_linear`` (tcgen05, split-K over a cluster).
+"""The decode-step projection ``nb_linear`` (tcgen05; 256-row weight tiles by
+default, 128-row tiles with or without a cluster split-K when forced).
 
 Every projection of a decode step of the benchmarked models, a few ragged
 shapes (N not a multiple of the 128-row tile, K not a multiple of 64, M
-from 1 to 256), strided x / y, bias, fp16, and every cluster size the host
-can pick, against a float32 matmul of the same 16-bit inputs.  Tolerance:
+from 1 to 256), strided x / y, bias, fp16, and every tile path, against a float32 matmul of the same 16-bit inputs.  Tolerance:
 the output is the fp32 sum rounded once to the 16-bit type, so it is within
 one unit in the last place of the reference plus the fp32 summation-order
 difference: |y - ref| <= 2^-7 |ref| + 2^-9 * max|ref| (bf16; a quarter of
 that for fp16).  Results are deterministic (same bits on a second call).
 """
-import os
-
 import pytest
 import torch
 
@@ -65,10 +63,13 @@ def test_linear_bf16(cuda, M, N, K):
 
 
 @pytest.mark.parametrize("split", ["1", "2", "3", "4"])
-@pytest.mark.parametrize("M,N,K", [(256, 6144, 4096), (100, 1000, 1000), (32, 256, 192)])
+@pytest.mark.parametrize("M,N,K", [(256, 6144, 4096), (100, 1000, 1000), (32, 256, 192),
+                                   (200, 28672, 512)])
 def test_linear_every_cluster_size(cuda, monkeypatch, split, M, N, K):
-    """Each S the host can choose, forced, gives the same numbers within the
-    tolerance (the partial sums meet in distributed shared memory)."""
+    """The 128-row tile paths, forced: no split with double-buffered
+    accumulators ("1") and the cluster split-K with S = 2, 3, 4 (the partial
+    sums meet in distributed shared memory); the default 256-row tiles are
+    what the other tests run."""
     ops = _ops()
     monkeypatch.setenv("NB_LINEAR_SPLIT", split)
     g = torch.Generator(device=cuda).manual_seed(5)
@@ -99,14 +100,18 @@ def test_linear_bias_strided_views(cuda, dt):
 
 
 def test_linear_is_used_by_the_model_layers(cuda):
-    """dense() takes the kernel for a decode batch and torch beyond 256 rows;
-    both agree with the reference."""
+    """dense() takes the kernel for a decode batch with many output features
+    and torch beyond 256 rows or for few features; all agree with the
+    reference."""
+    from needle_b200 import ops
     from needle_b200.layers.linear import dense
     g = torch.Generator(device=cuda).manual_seed(3)
-    w = (torch.randn(512, 256, device=cuda, generator=g) / 16).to(torch.bfloat16)
-    for M in (256, 300):
-        x = torch.randn(M, 256, device=cuda, generator=g).to(torch.bfloat16)
-        _check(dense(x, w), _ref(x, w, None), torch.bfloat16)
+    for N in (512, 28672):
+        w = (torch.randn(N, 256, device=cuda, generator=g) / 16).to(torch.bfloat16)
+        for M in (256, 300):
+            x = torch.randn(M, 256, device=cuda, generator=g).to(torch.bfloat16)
+            assert ops.linear_preferred(x, w) == (M <= 256 and N == 28672)
+            _check(dense(x, w), _ref(x, w, None), torch.bfloat16)
 
 
 def test_linear_rejects_unsupported(cuda):
