@@ -515,6 +515,27 @@ def _weights_read_per_step(runner) -> int:
     return n
 
 
+def _nb_linear_per_step(runner, B) -> int:
+    """Projections of one decode step (batch B) that run on this library's
+    GEMM (``ops.linear_preferred``, as ``layers.linear.dense`` decides)."""
+    from needle_b200 import ops
+    from needle_b200.layers import linear as lin
+    if not lin._LINEAR_TC:
+        return 0
+
+    def pref(w):
+        if w is None:
+            return False
+        return ops.linear_preferred(torch.empty(B, w.shape[1], dtype=w.dtype, device=w.device), w)
+    n = 0
+    for layer in runner.model.model.layers:
+        attn, mlp = layer.self_attn, layer.mlp
+        for w in (getattr(attn, "_qkv_w", None), attn.o_proj.weight, getattr(mlp, "_gu_w", None),
+                  mlp.down_proj.weight):
+            n += pref(w)
+    return n + pref(runner.model.lm_head.weight)
+
+
 MODEL_WORKLOADS = {
     # name: (preset, requests, prompt lo, prompt hi, output tokens, label)
     "llama8b": ("llama3-8b", 256, 128, 1024, 256, "config3"),
@@ -703,6 +724,7 @@ def run_model(args):
     step_bytes = w_bytes + avg_ctx_bytes
     peak, peak_src = measured_hbm_peak()
     bound = B * peak * 1e9 / step_bytes
+    n_lin = _nb_linear_per_step(runner, B)
     # ---- the all-reduce's share of the step (N > 1) -----------------------
     allreduce = None
     if ws > 1:
@@ -754,8 +776,10 @@ def run_model(args):
             # per layer the RoPE + KV write, paged decode (+ merge when split),
             # SwiGLU and two fused add+RMSNorm (post-attention, and the next
             # layer's input norm or the final norm; the fused all-reduce under
-            # TP), and the sampler
-            "gpu_launches": Kd * (cfg.num_hidden_layers * (5 + (1 if merges else 0)) + 3),
+            # TP), the sampler, and the projections on nb_linear
+            "gpu_launches": Kd * (cfg.num_hidden_layers * (5 + (1 if merges else 0)) + 3
+                                  + n_lin),
+            "nb_linear_per_step": n_lin,
             "clocks": clocks.summary(),
         }
     ctx_now = [len(s.token_ids) - 1 for s in seqs]
