@@ -53,16 +53,11 @@ constexpr int kLinW = 128 * 128;   // one 128-row weight sub-tile x 64 K x 2 B
 constexpr int kLinX = 256 * 128;   // up to 256 token rows x 64 K x 2 B
 // Pipeline depth: 4 stages of one sub-tile + x (48 KB), or 3 stages of two
 // sub-tiles + x (64 KB); 192 KB either way.
-// Two rings: the weight tiles (from HBM, long latency) get the deeper one,
-// the x tiles (re-read from L2 by every CTA, short latency) a shallower one,
-// each with its own producer warp, so the weight bytes in flight per SM are
-// not capped by the x ring: 128 KB of weights + 96 KB of x.
-template <int TW> constexpr int lin_wstages() { return TW == 2 ? 4 : 8; }
-constexpr int kLinXStages = 3;
-constexpr int kLinXRing = 128 * 1024;  // the x ring starts after 128 KB of weight stages
-constexpr int kLinBars = kLinXRing + kLinXStages * kLinX;  // 224 KB
-constexpr int kLinSmem = kLinBars + 512 + 1024;
-constexpr int kLinThreads = 224;
+template <int TW> constexpr int lin_stages() { return TW == 2 ? 3 : 4; }
+template <int TW> constexpr int lin_stage_bytes() { return TW * kLinW + kLinX; }
+constexpr int kLinBars = 192 * 1024;
+constexpr int kLinSmem = kLinBars + 256 + 1024;
+constexpr int kLinThreads = 192;
 constexpr int kLinChunk = 128 * 32 * 4;  // one 32-column chunk of a partial: 16 KB
 
 // TW: 128-row weight sub-tiles per tile (1 or 2; a tile is 128 TW output
@@ -74,9 +69,8 @@ __global__ void __launch_bounds__(kLinThreads, 1)
                      const T* __restrict__ bias, int M, int N, int NT, int n_tiles, int KB) {
   static_assert(S == 1 || TW == 1, "the cluster split takes one sub-tile per tile");
   constexpr bool kBf16 = !__is_same(T, __half);
-  constexpr int kWS = lin_wstages<TW>();
-  constexpr int kWStage = TW * kLinW;
-  constexpr int kXS = kLinXStages;
+  constexpr int kStages = lin_stages<TW>();
+  constexpr int kStage = lin_stage_bytes<TW>();
   // accumulator sets: two (double buffering) when a tile's accumulators fit
   // twice in tensor memory, else one
   constexpr int kNbuf = (S == 1 && TW == 1) ? 2 : 1;
@@ -85,17 +79,15 @@ __global__ void __launch_bounds__(kLinThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sb = smem_u32(smem);
-  const uint32_t bar_wfull = sb + kLinBars;       // [8] weight stage landed
-  const uint32_t bar_wempty = bar_wfull + 64;     // [8] weight stage read by its MMAs
-  const uint32_t bar_xfull = bar_wfull + 128;     // [4] x stage landed
-  const uint32_t bar_xempty = bar_wfull + 160;    // [4] x stage read by its MMAs
-  const uint32_t bar_acc = bar_wfull + 192;       // [2] accumulator set final
-  const uint32_t bar_accfree = bar_wfull + 208;   // [2] accumulator set read out (128 arrivals)
-  const uint32_t bar_ready = bar_wfull + 224;     // S > 1: the other CTAs' stages are free
-  const uint32_t bar_recv = bar_wfull + 232;      // S > 1: the other CTAs' chunks landed here
-  const uint32_t bar_end = bar_wfull + 240;       // every MMA of this CTA finished
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kLinBars + 256);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kLinBars + 264);
+  const uint32_t bar_full = sb + kLinBars;        // [4] stage landed
+  const uint32_t bar_empty = bar_full + 32;       // [4] stage read by its MMAs
+  const uint32_t bar_acc = bar_full + 64;         // [2] accumulator set final
+  const uint32_t bar_accfree = bar_full + 80;     // [2] accumulator set read out (128 arrivals)
+  const uint32_t bar_ready = bar_full + 96;       // S > 1: the other CTAs' stages are free
+  const uint32_t bar_recv = bar_full + 104;       // S > 1: the other CTAs' chunks landed here
+  const uint32_t bar_end = bar_full + 112;        // every MMA of this CTA finished
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kLinBars + 128);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kLinBars + 136);
   const uint32_t acc_cols = NT <= 128 ? 128u : 256u;  // one sub-tile's accumulator
   const uint32_t tmem_cols = kNbuf * TW * acc_cols;   // <= 512
   const int rank = S == 1 ? 0 : (int)cluster_ctarank();
@@ -107,13 +99,9 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&wmap);
     prefetch_tensormap(&xmap);
-    for (int i = 0; i < kWS; ++i) {
-      mbar_init(bar_wfull + 8 * i, 1);
-      mbar_init(bar_wempty + 8 * i, 1);
-    }
-    for (int i = 0; i < kXS; ++i) {
-      mbar_init(bar_xfull + 8 * i, 1);
-      mbar_init(bar_xempty + 8 * i, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(bar_full + 8 * i, 1);
+      mbar_init(bar_empty + 8 * i, 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_acc + 8 * i, 1);
@@ -135,51 +123,50 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   const int tstep = S == 1 ? (int)gridDim.x : n_tiles;
   const int kb0 = S == 1 ? 0 : rank * KB / S, kb1 = S == 1 ? KB : (rank + 1) * KB / S;
 
-  const int kper = kb1 - kb0;
-  const int n_mine = tile0 < n_tiles ? ((n_tiles - 1 - tile0) / tstep + 1) * kper : 0;
-  if (warp == 0 || warp == 6) {
-    // ---------------- TMA producers: warp 0 weights, warp 6 x ----------------
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      const bool is_w = warp == 0;
-      const int nst = is_w ? kWS : kXS;
-      const uint32_t bar_f = is_w ? bar_wfull : bar_xfull;
-      const uint32_t bar_e = is_w ? bar_wempty : bar_xempty;
-      const uint32_t bytes = is_w ? (uint32_t)kWStage : (uint32_t)NT * 128;
-      auto issue = [&](int j, uint32_t st) {
-        const int t = tile0 + (j / kper) * tstep, kb = kb0 + j % kper;
-        mbar_arrive_expect_tx(bar_f + 8 * st, bytes);
-        if (is_w) {
+      const uint32_t bytes = TW * kLinW + (uint32_t)NT * 128;
+      const int kper = kb1 - kb0;
+      const int n_mine = tile0 < n_tiles ? ((n_tiles - 1 - tile0) / tstep + 1) * kper : 0;
+      auto load_w = [&](uint32_t dst, int t, int kb, uint32_t bar) {
 #pragma unroll
-          for (int w = 0; w < TW; ++w)
-            tma_load_2d(sb + st * kWStage + w * kLinW, &wmap, kb * 64, (t * TW + w) * 128,
-                        bar_f + 8 * st);
-        } else {
-          tma_load_2d(sb + kLinXRing + st * kLinX, &xmap, kb * 64, 0, bar_f + 8 * st);
-        }
+        for (int w = 0; w < TW; ++w)
+          tma_load_2d(dst + w * kLinW, &wmap, kb * 64, (t * TW + w) * 128, bar);
       };
-      // The weights do not depend on the previous kernel: the first ring of
-      // weight tiles is requested before the programmatic-launch wait; the x
-      // tiles, the previous kernel's output, after it.
-      int j = 0;
-      if (is_w)
-        for (; j < n_mine && j < nst; ++j) issue(j, (uint32_t)j);
+      // The weights do not depend on the previous kernel: the first stages'
+      // weight tiles are requested before the programmatic-launch wait, the
+      // activation tiles after it.
+      const int pre = n_mine < kStages ? n_mine : kStages;
+      for (int j = 0; j < pre; ++j) {
+        mbar_arrive_expect_tx(bar_full + 8 * j, bytes);
+        load_w(sb + j * kStage, tile0 + (j / kper) * tstep, kb0 + j % kper, bar_full + 8 * j);
+      }
       griddep_wait();
+      for (int j = 0; j < pre; ++j)
+        tma_load_2d(sb + j * kStage + TW * kLinW, &xmap, (kb0 + j % kper) * 64, 0,
+                    bar_full + 8 * j);
+      uint32_t it = (uint32_t)pre;
       bool ok = true;
-      for (; ok && j < n_mine; ++j) {
-        const uint32_t st = (uint32_t)(j % nst), round = (uint32_t)(j / nst);
-        if (*abort_flag || !mbar_wait_bounded(bar_e + 8 * st, (round & 1) ^ 1)) {
+      for (int j = pre; ok && j < n_mine; ++j, ++it) {
+        const int t = tile0 + (j / kper) * tstep, kb = kb0 + j % kper;
+        const uint32_t st = it % kStages, round = it / kStages;
+        if (*abort_flag || !mbar_wait_bounded(bar_empty + 8 * st, (round & 1) ^ 1)) {
           ok = false;
           break;
         }
-        issue(j, st);
+        const uint32_t dst = sb + st * kStage;
+        mbar_arrive_expect_tx(bar_full + 8 * st, bytes);
+        load_w(dst, t, kb, bar_full + 8 * st);
+        tma_load_2d(dst + TW * kLinW, &xmap, kb * 64, 0, bar_full + 8 * st);
       }
       if (!ok) {
         *abort_flag = 1;
         set_error(kErrTimeout);
       }
       // copies still in flight land before the CTA moves on
-      for (int i = j > nst ? j - nst : 0; i < j; ++i)
-        mbar_wait_bounded(bar_f + 8 * (i % nst), (i / nst) & 1);
+      for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0; j < it; ++j)
+        mbar_wait_bounded(bar_full + 8 * (j % kStages), (j / kStages) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -199,14 +186,13 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + buf * TW * acc_cols;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const uint32_t sw = it % kWS, sx = it % kXS;
-          if (*abort_flag || !mbar_wait_bounded(bar_wfull + 8 * sw, (it / kWS) & 1) ||
-              !mbar_wait_bounded(bar_xfull + 8 * sx, (it / kXS) & 1)) {
+          const uint32_t st = it % kStages, round = it / kStages;
+          if (*abort_flag || !mbar_wait_bounded(bar_full + 8 * st, round & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a = sb + sw * kWStage, b = sb + kLinXRing + sx * kLinX;
+          const uint32_t a = sb + st * kStage, b = a + TW * kLinW;
 #pragma unroll
           for (int w = 0; w < TW; ++w)
 #pragma unroll
@@ -214,8 +200,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
               tc_mma_f16_ss(d + w * acc_cols, smem_desc_sw128(a + w * kLinW + kk * 32, 16, 1024),
                             smem_desc_sw128(b + kk * 32, 16, 1024), idesc,
                             (kb > kb0 || kk > 0) ? 1u : 0u);
-          tc_commit(bar_wempty + 8 * sw);  // the stages may be refilled
-          tc_commit(bar_xempty + 8 * sx);
+          tc_commit(bar_empty + 8 * st);  // the stage may be refilled
         }
         if (!ok) break;
         tc_commit(bar_acc + 8 * buf);
@@ -228,7 +213,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       mbar_wait_bounded(bar_end, 0);
     }
   } else {
-    // ---------------- epilogue (warps 2-5) ----------------
+    // ---------------- epilogue ----------------
     griddep_wait();
     const int q = warp & 3;
     const int nl = q * 32 + lane;  // this thread's output feature within a sub-tile

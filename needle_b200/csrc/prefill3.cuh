@@ -58,11 +58,6 @@ __device__ __forceinline__ float exp2_poly(float x) {
 #ifndef NB_PF3_POLY
 #define NB_PF3_POLY 0
 #endif
-// 1: the epilogue reads all of O_X before handing it back; 0 (default,
-// measured 3 % faster at 16 x 1024): chunk by chunk
-#ifndef NB_PF3_EPI_BATCH
-#define NB_PF3_EPI_BATCH 0
-#endif
 // threads per query row in the softmax groups (1 or 2)
 #ifndef NB_PF3_SPLIT_DEFAULT
 #define NB_PF3_SPLIT_DEFAULT 1
@@ -525,30 +520,6 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       const float inv = 1.f / l;
       T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)pf3_head(w, x, pair) * D +
                hsel * (D / SPLIT);
-#if NB_PF3_EPI_BATCH
-      // this thread's O columns in one batch of TMEM loads and one wait; O_X
-      // is handed back to the MMA warp before the conversion and the stores
-      uint32_t ov[OC][32];
-#pragma unroll
-      for (int c = 0; c < OC; ++c) tmem_ld32_nowait(tO + lane_off + c * 32, ov[c]);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
-      if (qi < len) {
-#pragma unroll
-        for (int c = 0; c < OC; ++c)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              pk[e] = Mma<T>::pack(__uint_as_float(ov[c][k * 8 + 2 * e]) * inv,
-                                   __uint_as_float(ov[c][k * 8 + 2 * e + 1]) * inv);
-            *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) =
-                make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          }
-      }
-#else
       // one 32-column chunk at a time: load, convert, store; O_X handed back
       // after the last chunk
 #pragma unroll 1
@@ -569,7 +540,6 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       }
       tc_fence_before();
       mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
-#endif
       ++nunits;
     }
     if (!ok) {

@@ -5,8 +5,8 @@ Mirrors ``needle/layers/linear.py:21-98``: ``ColumnParallelLinear`` holds
 ``RowParallelLinear`` holds ``weight[out, in/tp]`` and all-reduces (SUM) its
 output over the tensor-parallel group before adding the bias.  Every GEMM
 goes through ``dense``: decode-size batches (at most 256 rows, bf16 / fp16)
-with many output features (the gate/up projection, the LM head) on this
-library's tcgen05 kernel, everything else on torch (cuBLAS).  The
+of the LM head on this library's tcgen05 kernel, everything else on torch
+(cuBLAS), which measures faster for the narrower projections.  The
 all-reduce is NCCL through ``torch.distributed``, or, with a ``TPComm``
 attached, the fused all-reduce + residual + RMSNorm kernel run by the
 following ``RMSNorm``.

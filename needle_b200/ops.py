@@ -412,15 +412,16 @@ _SMS = {}
 
 def linear_preferred(x: torch.Tensor, weight: torch.Tensor) -> bool:
     """Whether ``linear`` is the faster choice for this GEMM on this GPU:
-    supported, and enough 256-row weight tiles (``N / 256``) to keep at
-    least 65 % of the SMs streaming weights.  Projections with fewer tiles
-    (Llama-3-8B qkv, o_proj, down at one GPU) measure faster on cuBLAS."""
+    supported, and at least three 256-row weight tiles per SM (an LM head:
+    128256 x 4096 measured 266 us against cuBLAS's 278 us at 256 rows).
+    Narrower projections measure faster on cuBLAS (gate/up 28672 x 4096:
+    79 vs 66 us; qkv, o_proj, down: 2-4x slower)."""
     if not linear_supported(x, weight):
         return False
     dev = x.device.index
     if dev not in _SMS:
         _SMS[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
-    return (weight.shape[0] + 255) // 256 >= 0.65 * _SMS[dev]
+    return (weight.shape[0] + 255) // 256 >= 3 * _SMS[dev]
 
 
 def swap_kv_blocks(src_caches, dst_caches, pairs: torch.Tensor) -> None:

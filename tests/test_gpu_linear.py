@@ -106,11 +106,11 @@ def test_linear_is_used_by_the_model_layers(cuda):
     from needle_b200 import ops
     from needle_b200.layers.linear import dense
     g = torch.Generator(device=cuda).manual_seed(3)
-    for N in (512, 28672):
+    for N in (512, 128256):
         w = (torch.randn(N, 256, device=cuda, generator=g) / 16).to(torch.bfloat16)
         for M in (256, 300):
             x = torch.randn(M, 256, device=cuda, generator=g).to(torch.bfloat16)
-            assert ops.linear_preferred(x, w) == (M <= 256 and N == 28672)
+            assert ops.linear_preferred(x, w) == (M <= 256 and N == 128256)
             _check(dense(x, w), _ref(x, w, None), torch.bfloat16)
 
 
