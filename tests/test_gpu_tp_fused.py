@@ -30,6 +30,9 @@ import torch
 pytestmark = pytest.mark.gpu
 
 HIDDEN = 1024
+# ranks of the op, mixed-shape and stress tests (NB_TP_TEST_WORLD, default 2;
+# 4 or 8 on a box with that many GPUs)
+WORLD = int(os.environ.get("NB_TP_TEST_WORLD", "2"))
 EPS = 1e-6
 ROWS = [1, 7, 64, 33, 2, 64]
 
@@ -150,9 +153,9 @@ def _run(target, world, extra=()):
 
 
 def test_fused_allreduce_rmsnorm_matches_cpu(cuda):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    res = _run(_op_worker, 2)
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    res = _run(_op_worker, WORLD)
     for r, (report, errs) in res.items():
         assert errs == 0, (r, errs)
         assert len(report) == len(ROWS) + 4
@@ -201,9 +204,9 @@ def _mixed_worker(rank, world, port, q):
 
 
 def test_fused_allreduce_mixed_launch_shapes(cuda):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    res = _run(_mixed_worker, 2)
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    res = _run(_mixed_worker, WORLD)
     for r, (report, errs) in res.items():
         assert errs == 0, (r, errs)
         for T, h_exact, y_err in report:
@@ -258,9 +261,9 @@ def _stress_worker(rank, world, port, q):
 
 
 def test_fused_allreduce_stress_mixed_shapes(cuda):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    res = _run(_stress_worker, 2)
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    res = _run(_stress_worker, WORLD)
     for r, (bad, checked, errs, poisoned) in res.items():
         assert errs == 0 and not poisoned, (r, errs)
         assert checked >= 10 and not bad, (r, bad)
