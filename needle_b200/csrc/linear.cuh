@@ -2,12 +2,14 @@
 // (+ bias[N]) for M <= 256 rows, bf16 / fp16 in, fp32 accumulation, output in
 // the input type.  Replaces the torch F.linear calls of needle's
 // ColumnParallelLinear / RowParallelLinear / QKV / gate-up / lm_head
-// (needle/layers/linear.py:21-98) when the batch is a decode step.
+// (needle/layers/linear.py:21-98) when the batch is a decode step; the model
+// routes only the LM head here (the shape where it measures faster than
+// cuBLAS).
 //
-// At M <= 256 the GEMM sits at the ridge of the roofline (2 FLOPs per weight
-// byte x 256 rows against ~250 FLOP/B), and a 128-row weight tile per CTA
-// gives only N / 128 tiles (qkv of Llama-3-8B: 48; o_proj and down: 32), far
-// fewer than the 148 SMs that must stream the weights.  So:
+// At M <= 256 the GEMM sits at the ridge of the roofline (M FLOPs per weight
+// byte: 256 against ~255 FLOP/B), and a 128-row weight tile per CTA gives
+// only N / 128 tiles (qkv of Llama-3-8B: 48; o_proj and down: 32), far fewer
+// than the 148 SMs that must stream the weights.  So:
 //
 //   * swap-AB: the MMA's M is 128 weight rows (A = W tile, K-major, 128-byte
 //     swizzled, as TMA writes it) and its N is the padded token count
@@ -20,14 +22,13 @@
 //     owner's shared memory (the freed pipeline stages), and each owner adds
 //     the other partials to its own in rank order and writes its chunks of y
 //     (a fixed order: the result is the same on every run; one tile per
-//     cluster, S chosen by the host from the tile and SM counts);
+//     cluster);
 //   * S = 1: persistent CTAs over tiles.  The default tile is 256 weight
 //     rows (two 128-row sub-tiles, two accumulators of all 512 TMEM columns)
-//     sharing each x tile: the weights are the only bytes that come from
-//     HBM, and at one CTA per SM the shared memory in flight (3 stages of
-//     64 KB) is what bounds a CTA's read rate, so the x share of every stage
-//     is kept to a half.  With 128-row tiles the two accumulator sets double-
-//     buffer instead, so the epilogue of one tile overlaps the next tile.
+//     sharing each x tile, so the x share of every stage (x is re-read from
+//     L2 by every CTA) is a half instead of two thirds.  With 128-row tiles
+//     the two accumulator sets double-buffer instead, so the epilogue of one
+//     tile overlaps the next tile.
 //   The cluster split-K path (128-row tiles) is kept for shapes with few
 //   tiles, selected explicitly: a cluster of S CTAs must be co-resident, and
 //   the number of co-resident clusters (45 clusters of 3 at 197 KB of shared

@@ -94,11 +94,13 @@ __global__ void __launch_bounds__(256)
   const int nwarps = gridDim.x * (blockDim.x >> 5);
   const int64_t half = (int64_t)num_blocks * kvh * block_size * D;
   const int64_t head = (int64_t)block_size * D;
-  for (int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < units; w += nwarps) {
-    const int t = w / upt;
+  // load(w): the unit's slot and source vectors; store(w): the vectors into
+  // the cache.  A warp's next unit is loaded before the current one is
+  // stored, so each warp keeps two units of reads in flight.
+  auto load = [&](int w, uint4 (&val)[U], int& t, int& slot) {
+    t = w / upt;
     const int j0 = (w - t * upt) * 32 * U;
-    const int slot = __ldg(slots + t);
-    uint4 val[U];
+    slot = __ldg(slots + t);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * 32 + lane;
@@ -109,18 +111,38 @@ __global__ void __launch_bounds__(256)
         val[u] = __ldg(reinterpret_cast<const uint4*>(src));
       }
     }
+  };
+  auto store = [&](int w, const uint4 (&val)[U], int t, int slot) {
+    const int j0 = (w - t * upt) * 32 * U;
     const int64_t base = slot_base(slot, num_blocks, kvh, block_size, D);
-    if (base >= 0) {
+    if (base < 0) return;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int j = j0 + u * 32 + lane;
-        if (j < per_tok) {
-          const int vec = j % vpr, r = j / vpr;
-          T* dst = cache + base + ((r & 1) ? half : 0) + (r >> 1) * head + vec * VEC;
-          *reinterpret_cast<uint4*>(dst) = val[u];
-        }
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + u * 32 + lane;
+      if (j < per_tok) {
+        const int vec = j % vpr, r = j / vpr;
+        T* dst = cache + base + ((r & 1) ? half : 0) + (r >> 1) * head + vec * VEC;
+        *reinterpret_cast<uint4*>(dst) = val[u];
       }
     }
+  };
+  int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= units) return;
+  uint4 cur[U];
+  int t = 0, slot = -1;
+  load(w, cur, t, slot);
+  while (true) {
+    const int wn = w + nwarps;
+    uint4 nxt[U];
+    int tn = 0, sn = -1;
+    if (wn < units) load(wn, nxt, tn, sn);
+    store(w, cur, t, slot);
+    if (wn >= units) break;
+    w = wn;
+    t = tn;
+    slot = sn;
+#pragma unroll
+    for (int u = 0; u < U; ++u) cur[u] = nxt[u];
   }
 }
 
@@ -215,20 +237,25 @@ __global__ void __launch_bounds__(256)
 namespace nbh {
 
 // Warps for `units` work units: enough CTAs of 8 warps for one unit per warp,
-// capped at a few resident waves (the kernels grid-stride).
+// capped at a few resident waves (the kernels grid-stride; NB_KVW_WAVES=1..4
+// sets the cap, diagnostics).
 inline unsigned slot_grid(int64_t units) {
-  const int64_t cap = (int64_t)num_sms() * 8 * 4;
+  static int waves = [] {
+    const char* e = getenv("NB_KVW_WAVES");
+    return (e && e[0] >= '1' && e[0] <= '4') ? e[0] - '0' : 4;
+  }();
+  const int64_t cap = (int64_t)num_sms() * 8 * waves;
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>((units + 7) / 8, cap));
 }
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-// 16-byte vectors per lane and unit of the slot writers: 4 or 8 (NB_KVW_U,
-// diagnostics).
+// 16-byte vectors per lane and unit of the slot writers: 2, 4 or 8
+// (NB_KVW_U, diagnostics).
 inline int kvw_unroll() {
   static int v = [] {
     const char* e = getenv("NB_KVW_U");
-    return (e && e[0] == '8') ? 8 : 4;
+    return (e && e[0] == '8') ? 8 : (e && e[0] == '2') ? 2 : 4;
   }();
   return v;
 }
@@ -260,6 +287,7 @@ int launch_store_slots(const void* k, int64_t ks, const void* v, int64_t vs, voi
     return check_launch("store_kvcache_slots");
   };
   if (kvw_unroll() == 8) return go(std::integral_constant<int, 8>());
+  if (kvw_unroll() == 2) return go(std::integral_constant<int, 2>());
   return go(std::integral_constant<int, 4>());
 }
 
