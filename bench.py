@@ -1292,8 +1292,8 @@ def run_kernel_cases(args):
              lambda: ops.silu_mul(gu, out=o))
     del x, r, w, o, ro, gu
     # paged decode: config 2 (tensor-core split + merge), GQA group 16 (32
-    # query / 2 KV heads: the tensor-core kernel in two 8-head chunks) and
-    # the SIMT kernel (fp32 cache, config-2 shape)
+    # query / 2 KV heads: the tensor-core kernel with 16-head tiles) and the
+    # SIMT kernel (fp32 cache, config-2 shape)
     for kvh, tag, kern, dt in (
             (8, "config 2 (group 4)", "paged_decode_tc_kernel + decode_merge_kernel", bf),
             (2, "group 16 (32/2 heads)", "paged_decode_tc_kernel + decode_merge_kernel", bf),

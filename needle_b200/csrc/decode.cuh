@@ -58,7 +58,9 @@ __device__ __forceinline__ void decode_extent(int ctx, int maxb, int bs, int pps
   if (n_splits < 1) n_splits = 1;
 }
 
-template <typename T, int D, int WARPS, int STAGES>
+// NH: 8-head MMA column tiles per CTA (1: up to 8 query heads of a KV head;
+// 2: up to 16, for groups above 8, so each page is read by one CTA).
+template <typename T, int D, int WARPS, int STAGES, int NH>
 __global__ void __launch_bounds__(WARPS * 32)
     paged_decode_tc_kernel(const __grid_constant__ CUtensorMap kv_map, const T* __restrict__ q,
                            int64_t q_sb, int64_t q_sh, const int32_t* __restrict__ bt,
@@ -78,13 +80,14 @@ __global__ void __launch_bounds__(WARPS * 32)
                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  // grid.y = kv head x chunks of up to 8 query heads of its group: groups
-  // above 8 run as several CTAs that read the same pages (adjacent in the
+  // grid.y = kv head x chunks of up to 8 NH query heads of its group: groups
+  // above 8 NH run as several CTAs that read the same pages (adjacent in the
   // grid, so the second read of a page is usually an L2 hit)
-  const int nhc = (group + 7) >> 3;
+  constexpr int HN = 8 * NH;  // query heads per CTA
+  const int nhc = (group + HN - 1) / HN;
   const int split = blockIdx.x, h = blockIdx.y / nhc, b = blockIdx.z;
-  const int n0 = (blockIdx.y - h * nhc) * 8;
-  const int gcount = min(8, group - n0);
+  const int n0 = (blockIdx.y - h * nhc) * HN;
+  const int gcount = min(HN, group - n0);
   const int ctx = __ldg(ctx_lens + b);
   if (ctx < 0 && threadIdx.x == 0 && split == 0 && n0 == 0) set_error(kErrPosition);
   int n_tok, n_pages, n_splits;
@@ -136,22 +139,32 @@ __global__ void __launch_bounds__(WARPS * 32)
     if (lane == 0 && i < n_w) issue(i, row);
   }
 
-  // Q^T as the B operand (k = d, n = head): lane holds heads g, d pairs 2*t4.
-  uint32_t qf[NK][2];
-  {
-    const bool hv = g < gcount;
-    const T* qrow = q + (int64_t)b * q_sb + (int64_t)(h * group + n0 + (hv ? g : 0)) * q_sh;
+  // Q^T as the B operand (k = d, n = head): in column tile nt, lane holds
+  // head 8 nt + g, d pairs 2*t4.
+  uint32_t qf[NH][NK][2];
+#pragma unroll
+  for (int nt = 0; nt < NH; ++nt) {
+    const bool hv = 8 * nt + g < gcount;
+    const T* qrow =
+        q + (int64_t)b * q_sb + (int64_t)(h * group + n0 + (hv ? 8 * nt + g : 0)) * q_sh;
 #pragma unroll
     for (int kk = 0; kk < NK; ++kk) {
-      qf[kk][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4)) : 0u;
-      qf[kk][1] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * t4)) : 0u;
+      qf[nt][kk][0] =
+          hv ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4)) : 0u;
+      qf[nt][kk][1] =
+          hv ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * t4)) : 0u;
     }
   }
 
-  float o[NK][4];
+  float o[NH][NK][4];
+  float m0[NH], m1[NH], l0[NH], l1[NH];
 #pragma unroll
-  for (int mt = 0; mt < NK; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  for (int nt = 0; nt < NH; ++nt) {
+#pragma unroll
+    for (int mt = 0; mt < NK; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
+    m0[nt] = m1[nt] = -INFINITY;
+    l0[nt] = l1[nt] = 0.f;
+  }
   const int mi = lane >> 3;
   bool ok = true;
   int consumed = 0;
@@ -164,52 +177,65 @@ __global__ void __launch_bounds__(WARPS * 32)
     const uint32_t kb = wbase_u + s * G::kStageBytes;
     const uint32_t vb = kb + G::kPageBytes;
 
-    // S^T = K . Q^T  (16 tokens x 8 heads)
-    // two independent accumulation chains halve the MMA dependency depth
-    float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
+    // S^T = K . Q^T  (16 tokens x 8 NH heads); the K fragments serve every
+    // column tile; two independent accumulation chains per tile halve the
+    // MMA dependency depth
+    float sc[NH][4], sd[NH][4];
+#pragma unroll
+    for (int nt = 0; nt < NH; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] = sd[nt][e] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < NK; kk += 2) {
       uint32_t a[4], a2[4];
       ldmatrix_x4(a, swz_addr(kb, (lane & 7) + ((mi & 1) << 3), kk * 2 + (mi >> 1)));
       ldmatrix_x4(a2, swz_addr(kb, (lane & 7) + ((mi & 1) << 3), kk * 2 + 2 + (mi >> 1)));
-      Mma<T>::run(sc, a, qf[kk][0], qf[kk][1]);
-      Mma<T>::run(sd, a2, qf[kk + 1][0], qf[kk + 1][1]);
-    }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) sc[e] += sd[e];
+      for (int nt = 0; nt < NH; ++nt) {
+        Mma<T>::run(sc[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+        Mma<T>::run(sd[nt], a2, qf[nt][kk + 1][0], qf[nt][kk + 1][1]);
+      }
+    }
     const int tok = (p0 + warp + WARPS * i) * 16 + g;
-    const float x0 = tok < n_tok ? sc[0] * scale_log2 : -INFINITY;
-    const float x1 = tok < n_tok ? sc[1] * scale_log2 : -INFINITY;
-    const float x2 = tok + 8 < n_tok ? sc[2] * scale_log2 : -INFINITY;
-    const float x3 = tok + 8 < n_tok ? sc[3] * scale_log2 : -INFINITY;
-    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+    uint32_t pb0[NH], pb1[NH];
 #pragma unroll
-    for (int sh = 4; sh < 32; sh <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
-    }
-    // every page holds at least one valid token, so mx is finite
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-    const float e0 = exp2f(x0 - mn0), e1 = exp2f(x1 - mn1);
-    const float e2 = exp2f(x2 - mn0), e3 = exp2f(x3 - mn1);
-    l0 = l0 * al0 + (e0 + e2);
-    l1 = l1 * al1 + (e1 + e3);
-    m0 = mn0;
-    m1 = mn1;
+    for (int nt = 0; nt < NH; ++nt) {
 #pragma unroll
-    for (int mt = 0; mt < NK; ++mt) {
-      o[mt][0] *= al0; o[mt][1] *= al1; o[mt][2] *= al0; o[mt][3] *= al1;
+      for (int e = 0; e < 4; ++e) sc[nt][e] += sd[nt][e];
+      const float x0 = tok < n_tok ? sc[nt][0] * scale_log2 : -INFINITY;
+      const float x1 = tok < n_tok ? sc[nt][1] * scale_log2 : -INFINITY;
+      const float x2 = tok + 8 < n_tok ? sc[nt][2] * scale_log2 : -INFINITY;
+      const float x3 = tok + 8 < n_tok ? sc[nt][3] * scale_log2 : -INFINITY;
+      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int sh = 4; sh < 32; sh <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
+      }
+      // every page holds at least one valid token, so mx is finite
+      const float mn0 = fmaxf(m0[nt], mx0), mn1 = fmaxf(m1[nt], mx1);
+      const float al0 = exp2f(m0[nt] - mn0), al1 = exp2f(m1[nt] - mn1);
+      const float e0 = exp2f(x0 - mn0), e1 = exp2f(x1 - mn1);
+      const float e2 = exp2f(x2 - mn0), e3 = exp2f(x3 - mn1);
+      l0[nt] = l0[nt] * al0 + (e0 + e2);
+      l1[nt] = l1[nt] * al1 + (e1 + e3);
+      m0[nt] = mn0;
+      m1[nt] = mn1;
+#pragma unroll
+      for (int mt = 0; mt < NK; ++mt) {
+        o[nt][mt][0] *= al0; o[nt][mt][1] *= al1; o[nt][mt][2] *= al0; o[nt][mt][3] *= al1;
+      }
+      // P^T as the B operand (k = token, n = head)
+      pb0[nt] = movmatrix_trans(Mma<T>::pack(e0, e1));
+      pb1[nt] = movmatrix_trans(Mma<T>::pack(e2, e3));
     }
-    // P^T as the B operand (k = token, n = head)
-    const uint32_t pb0 = movmatrix_trans(Mma<T>::pack(e0, e1));
-    const uint32_t pb1 = movmatrix_trans(Mma<T>::pack(e2, e3));
-    // O^T += V^T . P^T   (D x 8)
+    // O^T += V^T . P^T   (D x 8 NH); the V fragments serve every column tile
 #pragma unroll
     for (int mt = 0; mt < NK; ++mt) {
       uint32_t a[4];
       ldmatrix_x4_trans(a, swz_addr(vb, (lane & 7) + ((mi >> 1) << 3), mt * 2 + (mi & 1)));
-      Mma<T>::run(o[mt], a, pb0, pb1);
+#pragma unroll
+      for (int nt = 0; nt < NH; ++nt) Mma<T>::run(o[nt][mt], a, pb0[nt], pb1[nt]);
     }
     __syncwarp();
     const int nxt = i + STAGES;
@@ -230,10 +256,12 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 
 #pragma unroll
-  for (int sh = 4; sh < 32; sh <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, sh);
-  }
+  for (int nt = 0; nt < NH; ++nt)
+#pragma unroll
+    for (int sh = 4; sh < 32; sh <<= 1) {
+      l0[nt] += __shfl_xor_sync(0xffffffffu, l0[nt], sh);
+      l1[nt] += __shfl_xor_sync(0xffffffffu, l1[nt], sh);
+    }
 
   // Let the merge kernel (launched with programmatic stream serialisation)
   // get scheduled while this grid drains; it waits for our completion before
@@ -242,22 +270,26 @@ __global__ void __launch_bounds__(WARPS * 32)
 
   // In-CTA merge of the warps through shared memory (pipeline slots reused).
   __syncthreads();
-  float* sm_o = reinterpret_cast<float*>(smem);            // [warps][8][D]
-  float* sm_m = sm_o + WARPS * 8 * D;                    // [warps][8]
-  float* sm_l = sm_m + WARPS * 8;
+  float* sm_o = reinterpret_cast<float*>(smem);            // [warps][HN][D]
+  float* sm_m = sm_o + WARPS * HN * D;                   // [warps][HN]
+  float* sm_l = sm_m + WARPS * HN;
 #pragma unroll
-  for (int mt = 0; mt < NK; ++mt) {
-    const int d = mt * 16 + g;
-    sm_o[(warp * 8 + 2 * t4) * D + d] = o[mt][0];
-    sm_o[(warp * 8 + 2 * t4 + 1) * D + d] = o[mt][1];
-    sm_o[(warp * 8 + 2 * t4) * D + d + 8] = o[mt][2];
-    sm_o[(warp * 8 + 2 * t4 + 1) * D + d + 8] = o[mt][3];
-  }
-  if (g == 0) {
-    sm_m[warp * 8 + 2 * t4] = m0;
-    sm_m[warp * 8 + 2 * t4 + 1] = m1;
-    sm_l[warp * 8 + 2 * t4] = l0;
-    sm_l[warp * 8 + 2 * t4 + 1] = l1;
+  for (int nt = 0; nt < NH; ++nt) {
+    const int r0 = warp * HN + 8 * nt + 2 * t4;  // heads 8 nt + 2 t4, + 1
+#pragma unroll
+    for (int mt = 0; mt < NK; ++mt) {
+      const int d = mt * 16 + g;
+      sm_o[r0 * D + d] = o[nt][mt][0];
+      sm_o[(r0 + 1) * D + d] = o[nt][mt][1];
+      sm_o[r0 * D + d + 8] = o[nt][mt][2];
+      sm_o[(r0 + 1) * D + d + 8] = o[nt][mt][3];
+    }
+    if (g == 0) {
+      sm_m[r0] = m0[nt];
+      sm_m[r0 + 1] = m1[nt];
+      sm_l[r0] = l0[nt];
+      sm_l[r0 + 1] = l1[nt];
+    }
   }
   __syncthreads();
   const int H = kvh * group;
@@ -265,14 +297,14 @@ __global__ void __launch_bounds__(WARPS * 32)
     const int n = idx / D, d = idx - n * D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, sm_m[w * 8 + n]);
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, sm_m[w * HN + n]);
     float L = 0.f, O = 0.f;
 #pragma unroll
     for (int w = 0; w < WARPS; ++w) {
-      const float mw = sm_m[w * 8 + n];
+      const float mw = sm_m[w * HN + n];
       const float e = mw == -INFINITY ? 0.f : exp2f(mw - M);
-      L += sm_l[w * 8 + n] * e;
-      O += sm_o[(w * 8 + n) * D + d] * e;
+      L += sm_l[w * HN + n] * e;
+      O += sm_o[(w * HN + n) * D + d] * e;
     }
     const int qh = h * group + n0 + n;
     if (n_splits == 1) {
@@ -495,6 +527,14 @@ inline TcCfg decode_cfg() {
   return cfg;
 }
 
+inline bool decode_n16_enabled() {
+  static int on = [] {
+    const char* e = getenv("NB_DECODE_N16");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
+}
+
 template <typename T, int D, int WARPS, int STAGES>
 int launch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t qsh,
                      const int32_t* bt, int64_t bts, int maxb, const int32_t* ctx, int kvh,
@@ -503,12 +543,17 @@ int launch_decode_tc(const CUtensorMap& map, const void* q, int64_t qsb, int64_t
   using G = nb::TcGeom<D>;
   const size_t smem =
       1024 + (size_t)WARPS * STAGES * G::kStageBytes + (size_t)WARPS * STAGES * 8;
-  auto kern = nb::paged_decode_tc_kernel<T, D, WARPS, STAGES>;
+  // groups above 8: 16 heads per CTA (two MMA column tiles), so a page is
+  // read by one CTA (NB_DECODE_N16=0 keeps 8-head chunks; diagnostics)
+  const bool n16 = group > 8 && decode_n16_enabled();
+  auto kern = n16 ? nb::paged_decode_tc_kernel<T, D, WARPS, STAGES, 2>
+                  : nb::paged_decode_tc_kernel<T, D, WARPS, STAGES, 1>;
   if (int rc = ensure_max_smem((const void*)kern, (int)smem, "paged_decode_tc")) return rc;
+  const int hn = n16 ? 16 : 8;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
-  pdl_config(cfg, attr, dim3(max_splits, kvh * ((group + 7) / 8), B), dim3(WARPS * 32), smem,
-             st);
+  pdl_config(cfg, attr, dim3(max_splits, kvh * ((group + hn - 1) / hn), B), dim3(WARPS * 32),
+             smem, st);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, map, (const T*)q, qsb, qsh, bt, bts, maxb,
                                            ctx, kvh, group, nblk, scale_log2, pps, (T*)out, osb,
                                            osh, po, pml, max_splits);

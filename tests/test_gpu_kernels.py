@@ -249,8 +249,8 @@ def test_decode_vs_needle_golden(cuda, dt, H, kv, D, pps):
                                     (8, 8, 128), (12, 4, 96), (48, 2, 128), (20, 1, 64)])
 def test_decode_random_shapes(cuda, dt, H, kv, D):
     """Group sizes 4, 7, 8, 16, 24 and 20 (beyond one MMA tile: the tensor-core
-    kernel takes 8 query heads per CTA, the last chunk partial), MHA and an
-    odd head_dim."""
+    kernel takes 16 query heads per CTA in two column tiles, the last chunk
+    partial), MHA and an odd head_dim."""
     ops = _ops()
     g = torch.Generator().manual_seed(15)
     B, N, maxb = 9, 400, 40
@@ -264,6 +264,41 @@ def test_decode_random_shapes(cuda, dt, H, kv, D):
         out = ops.paged_decode(q.to(cuda), cache.to(cuda), bt.to(cuda), ctx.to(cuda),
                                1 / math.sqrt(D), plan=plan)
         assert _maxdiff(out, ref) <= ATOL[dt], (pps, _maxdiff(out, ref))
+
+
+_DECODE_8HEAD_CHECK = r"""
+import math, sys, torch
+sys.path.insert(0, '.')
+from needle_b200 import ops
+from oracle import needle_oracle as no
+g = torch.Generator().manual_seed(17)
+for H, kv, D in ((48, 2, 128), (20, 1, 64), (32, 2, 128)):
+    B, N, maxb = 5, 300, 30
+    ctx = torch.tensor([0, 16, 17, 300, 470], dtype=torch.int32)
+    bt = torch.randperm(N, generator=g)[: B * maxb].view(B, maxb).to(torch.int32)
+    q = torch.randn(B, H, D, generator=g).to(torch.bfloat16)
+    cache = torch.randn(2, N, kv, 16, D, generator=g).to(torch.bfloat16)
+    ref = no.decode_attention(q.float(), cache.float(), bt, ctx, 1 / math.sqrt(D), H, kv, D)
+    dev = torch.device('cuda:0')
+    out = ops.paged_decode(q.to(dev), cache.to(dev), bt.to(dev), ctx.to(dev), 1 / math.sqrt(D))
+    err = (out.float().cpu() - ref.float()).abs().max().item()
+    assert err <= 2e-2, (H, kv, D, err)
+assert ops.device_errors() == 0
+print('ok')
+"""
+
+
+def test_decode_large_groups_in_8_head_chunks(cuda):
+    """Groups above 8 with the 16-head tiles switched off (NB_DECODE_N16=0, a
+    fresh process): 8-head chunks, several CTAs per KV head."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NB_DECODE_N16="0")
+    r = subprocess.run([sys.executable, "-c", _DECODE_8HEAD_CHECK], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
 
 
 def test_decode_table_width_limits_context(cuda):
