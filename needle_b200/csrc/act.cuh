@@ -14,6 +14,9 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(256)
     silu_mul_kernel(const T* __restrict__ in, int64_t in_stride, T* __restrict__ out,
                     int64_t out_stride, int inter, int64_t total_vec) {
+  // programmatic launch, as rmsnorm_kernel
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= total_vec) return;
   const int vpr = inter / VEC;
@@ -60,15 +63,14 @@ int launch_silu_mul(const void* in, int64_t is, void* out, int64_t os, int T_, i
   const bool vec = inter % V16 == 0 && is % V16 == 0 && os % V16 == 0 &&
                    (uintptr_t)in % 16 == 0 && (uintptr_t)out % 16 == 0;
   const int threads = 256;
-  if (vec) {
-    const int64_t total = (int64_t)T_ * (inter / V16);
-    nb::silu_mul_kernel<T, V16><<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
-        (const T*)in, is, (T*)out, os, inter, total);
-  } else {
-    const int64_t total = (int64_t)T_ * inter;
-    nb::silu_mul_kernel<T, 1><<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
-        (const T*)in, is, (T*)out, os, inter, total);
-  }
+  const int64_t total = (int64_t)T_ * (vec ? inter / V16 : inter);
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, dim3((unsigned)((total + threads - 1) / threads)), dim3(threads), 0, st);
+  auto kern = vec ? nb::silu_mul_kernel<T, V16> : nb::silu_mul_kernel<T, 1>;
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, kern, (const T*)in, is, (T*)out, os, inter, total);
+  if (e != cudaSuccess) return fail(NB_ERR_CUDA, "silu_mul launch: %s", cudaGetErrorString(e));
   return check_launch("silu_mul");
 }
 

@@ -18,6 +18,10 @@ template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(1024)
     rmsnorm_kernel(const T* x, int64_t xs, const T* res, int64_t rs, const T* __restrict__ w,
                    T* out, int64_t os, T* res_out, int64_t ros, int hidden, float eps) {
+  // launched with programmatic stream serialisation: the launch overlaps the
+  // previous kernel's tail; every read waits for that kernel's results
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const T* xr = x + (int64_t)row * xs;
@@ -159,14 +163,13 @@ int launch_norm(const void* x, int64_t xs, const void* res, int64_t rs, const vo
   const int nvec = vec_ok ? hidden / V16 : hidden;
   int threads = 32;
   while (threads < 1024 && threads < nvec) threads *= 2;
-  if (vec_ok)
-    nb::rmsnorm_kernel<T, V16, ADD><<<T_, threads, 0, st>>>((const T*)x, xs, (const T*)res, rs,
-                                                            (const T*)w, (T*)out, os, (T*)ro, ros,
-                                                            hidden, eps);
-  else
-    nb::rmsnorm_kernel<T, 1, ADD><<<T_, threads, 0, st>>>((const T*)x, xs, (const T*)res, rs,
-                                                          (const T*)w, (T*)out, os, (T*)ro, ros,
-                                                          hidden, eps);
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, dim3(T_), dim3(threads), 0, st);
+  auto kern = vec_ok ? nb::rmsnorm_kernel<T, V16, ADD> : nb::rmsnorm_kernel<T, 1, ADD>;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const T*)x, xs, (const T*)res, rs,
+                                           (const T*)w, (T*)out, os, (T*)ro, ros, hidden, eps);
+  if (e != cudaSuccess) return fail(NB_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));
   return check_launch(ADD ? "fused_add_rmsnorm" : "rmsnorm");
 }
 
