@@ -1343,10 +1343,6 @@ def run_kernel_cases(args):
              lambda: torch.nn.functional.linear(xin, wgt))
         case(f"nb_linear M=256 {name}", "linear_tc_kernel", N_ * K_ * 2,
              lambda: ops.linear(xin, wgt, out=yout))
-        # the same product asked of cuBLAS as y^T = W x^T (weights as the
-        # left operand, written through the transposed view of y)
-        case(f"cuBLAS swapped M=256 {name}", "cuBLAS (torch.mm, W x^T)", N_ * K_ * 2,
-             lambda: torch.mm(wgt, xin.t(), out=yout.t()))
         del wgt, xin, yout
     torch.cuda.empty_cache()
     # the batched sampler at the config 3 decode shape (256 x 128256 bf16):
