@@ -343,6 +343,29 @@ NB_API int nb_sample(const void* logits, int64_t row_stride, int num_rows, int v
                      int64_t* token_ids, int dtype, void* stream);
 
 /*
+ * Paged prefill: causal attention of the new tokens of each sequence over
+ * the sequence's whole context — the context_lens[s] tokens already cached
+ * and the new tokens themselves — read from the paged cache
+ * [2, num_blocks, num_kv_heads, 16, head_dim] through the block table (the
+ * new tokens' K/V must have been written first, e.g. by
+ * nb_rope_store_kvcache_slots).  Query row i of sequence s sits at position
+ * context_lens[s] + i and sees keys 0 .. context_lens[s] + i.  With every
+ * context_lens[s] == 0 the result is nb_prefill_attention's.  This is the
+ * continuation case needle's own prefill does not handle (it attends over
+ * the new tokens only: needle/layers/attention.py:101-134, and its TODO.md
+ * lists the gap); decode attends over the cached tokens the same way
+ * (attention.py:291-310), so a chunk of n new tokens equals n decode steps.
+ * bf16 / fp16, head_dim 64 or 128, tcgen05; NB_ERR_UNSUPPORTED otherwise.
+ */
+NB_API int nb_prefill_attention_paged(const void* q, int64_t q_stride, const void* kv_cache,
+                                      int num_blocks, int num_kv_heads, const int32_t* block_table,
+                                      int64_t bt_stride, int max_blocks,
+                                      const int32_t* context_lens, int num_q_heads, int head_dim,
+                                      const int32_t* cu_seqlens, int num_seqs, int num_tokens,
+                                      int max_seqlen, float scale, void* out, int64_t out_stride,
+                                      int dtype, void* stream);
+
+/*
  * Dense projection of a decode step: y[M, N] = x[M, K] . weight[N, K]^T
  * (+ bias[N] when bias is not NULL), fp32 accumulation, output rounded to
  * the input dtype (bf16 or fp16).  Replaces the F.linear of needle's

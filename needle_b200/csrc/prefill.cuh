@@ -738,4 +738,45 @@ int nb_prefill_attention(const void* q, int64_t q_stride, const void* k, int64_t
   }
 }
 
+int nb_prefill_attention_paged(const void* q, int64_t q_stride, const void* kv_cache,
+                               int num_blocks, int num_kv_heads, const int32_t* block_table,
+                               int64_t bt_stride, int max_blocks, const int32_t* context_lens,
+                               int num_q_heads, int head_dim, const int32_t* cu_seqlens,
+                               int num_seqs, int num_tokens, int max_seqlen, float scale,
+                               void* out, int64_t out_stride, int dtype, void* stream) {
+  using namespace nbh;
+  if (dtype != NB_DTYPE_BF16 && dtype != NB_DTYPE_F16)
+    return fail(NB_ERR_UNSUPPORTED, "paged prefill takes bf16 or fp16");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(NB_ERR_UNSUPPORTED, "paged prefill takes head_dim 64 or 128 (got %d)", head_dim);
+  if (!q || !kv_cache || !block_table || !context_lens || !cu_seqlens || !out)
+    return fail(NB_ERR_INVALID_ARG, "null pointer");
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 || max_blocks <= 0 ||
+      num_seqs < 0 || num_tokens < 0 || bt_stride < max_blocks)
+    return fail(NB_ERR_INVALID_ARG, "bad sizes");
+  if (num_q_heads % num_kv_heads)
+    return fail(NB_ERR_INVALID_ARG, "num_q_heads not a multiple of num_kv_heads");
+  if (q_stride < (int64_t)num_q_heads * head_dim || out_stride < (int64_t)num_q_heads * head_dim)
+    return fail(NB_ERR_INVALID_ARG, "row stride too small");
+  if ((int64_t)2 * num_blocks * num_kv_heads * 16 > INT32_MAX)
+    return fail(NB_ERR_UNSUPPORTED, "cache rows exceed int32");
+  if (num_seqs == 0 || num_tokens == 0) return NB_OK;
+  if (max_seqlen <= 0) return fail(NB_ERR_INVALID_ARG, "max_seqlen must be > 0");
+  if ((q_stride * 2) % 16 || (out_stride * 2) % 16 || (uintptr_t)q % 16 || (uintptr_t)out % 16 ||
+      (uintptr_t)kv_cache % 16)
+    return fail(NB_ERR_UNSUPPORTED, "paged prefill needs 16-byte aligned rows");
+  const int group = num_q_heads / num_kv_heads;
+  const float sl2 = scale * nb::kLog2e;
+  cudaStream_t st = (cudaStream_t)stream;
+#define NB_PARGS q, q_stride, kv_cache, num_blocks, num_kv_heads, num_q_heads, group, block_table, \
+                 bt_stride, max_blocks, context_lens, cu_seqlens, num_seqs, num_tokens,         \
+                 max_seqlen, sl2, out, out_stride, dtype, st
+  if (dtype == NB_DTYPE_BF16)
+    return head_dim == 64 ? launch_prefill_tc3_paged<__nv_bfloat16, 64>(NB_PARGS)
+                          : launch_prefill_tc3_paged<__nv_bfloat16, 128>(NB_PARGS);
+  return head_dim == 64 ? launch_prefill_tc3_paged<__half, 64>(NB_PARGS)
+                        : launch_prefill_tc3_paged<__half, 128>(NB_PARGS);
+#undef NB_PARGS
+}
+
 }  // extern "C"

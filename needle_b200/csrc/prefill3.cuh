@@ -104,6 +104,19 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// Paged mode: K and V come from the paged cache [2, N, kvh, 16, D] through
+// the block table (keys 0 .. ctx + len - 1 of a sequence: the cached prefix
+// and the new tokens, whose rows the KV writer stored first), and query row i
+// of a sequence sits at absolute position ctx + i.  bt == nullptr: K and V
+// are the new tokens' contiguous rows and ctx = 0 (needle's prefill).
+struct Pf3Paged {
+  const int32_t* bt;    // [B, bt_stride] block ids
+  int64_t bt_stride;
+  int maxb;             // block-table columns
+  const int32_t* ctx;   // [B] cached tokens before the new ones
+  int num_blocks, kvh;
+};
+
 // Work unit u -> (query block, head, sequence); units with the most KV tiles
 // come first.  Units past a sequence's end are empty (every role skips them).
 // Two ways to give the two softmax groups their 128-row query tiles:
@@ -138,7 +151,7 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
                        const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
                        int B, int hq, int group, int nqb, int pair, float scale_log2,
-                       T* __restrict__ out, int64_t os) {
+                       T* __restrict__ out, int64_t os, const Pf3Paged pg) {
   using G = Pf3Geom<D>;
   constexpr bool kBf16 = !__is_same(T, __half);
   constexpr uint32_t kIdS = idesc_f16_f32(kBf16, 128, 128, false, false);
@@ -193,19 +206,31 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
   const uint32_t tmem = *tmem_slot;
   const int n_units = nqb * (pair ? hq / 2 : hq) * B;
 
-  // Causal extent of a unit: KV tiles under tile A / tile B (0: no tile B).
-  auto extent = [&](const Pf3Unit& w, int& s0, int& len, int& nA, int& nB) -> bool {
+  const bool paged = pg.bt != nullptr;
+  // Causal extent of a unit: KV tiles under tile A / tile B (0: no tile B);
+  // c = the sequence's cached prefix (keys before its new tokens)
+  auto extent = [&](const Pf3Unit& w, int& s0, int& len, int& nA, int& nB, int& c) -> bool {
     s0 = __ldg(cu + w.b);
     len = __ldg(cu + w.b + 1) - s0;
+    c = paged ? max(0, __ldg(pg.ctx + w.b)) : 0;
     const int q0 = pf3_row(w, 0, pair);
     if (q0 >= len) return false;
-    if (pair) {
-      nA = nB = w.qb + 1;
-    } else {
-      nA = 2 * w.qb + 1;
-      nB = q0 + 128 < len ? 2 * w.qb + 2 : 0;
-    }
+    const int q1 = pf3_row(w, 1, pair);
+    nA = (min(c + q0 + 127, c + len - 1) >> 7) + 1;
+    nB = q1 < len ? (min(c + q1 + 127, c + len - 1) >> 7) + 1 : 0;
     return true;
+  };
+  // paged mode: first cache row (K half) of page p of sequence b for KV head
+  // kh, or -16 (a box wholly before the tensor: TMA fills zeros) for a page
+  // past the table or an invalid block id (recorded)
+  auto page_row = [&](int b, int p, int kh) -> int {
+    if (p >= pg.maxb) return -16;
+    const int phys = __ldg(pg.bt + (int64_t)b * pg.bt_stride + p);
+    if (phys < 0 || phys >= pg.num_blocks) {
+      set_error(kErrBlockId);
+      return -16;
+    }
+    return (phys * pg.kvh + kh) * 16;
   };
 
   if (warp == 0) {
@@ -215,8 +240,8 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
         const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
-        int s0, len, nA, nB;
-        if (!extent(w, s0, len, nA, nB)) continue;
+        int s0, len, nA, nB, c;
+        if (!extent(w, s0, len, nA, nB, c)) continue;
         const int kh = w.h / group;
         const int n_kv = nB ? nB : nA;
         if (nq > 0 && !mbar_wait_bounded(bar_qfree, (nq - 1) & 1)) { ok = false; break; }
@@ -237,11 +262,27 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
             ok = false;
             break;
           }
+          // paged: the tile's 8 pages (16 keys each) through the block table;
+          // a 16-row box at a 16-row offset keeps the 128-byte swizzle of the
+          // 128-row tile
+          int prow[8];
+          if (paged) {
+#pragma unroll
+            for (int pp = 0; pp < 8; ++pp) prow[pp] = page_row(w.b, j * 8 + pp, kh);
+          }
+          const int v_off = paged ? pg.num_blocks * pg.kvh * 16 : 0;
           mbar_arrive_expect_tx(bar_k + 8 * st, G::kTile);
 #pragma unroll
-          for (int a = 0; a < D / 64; ++a)
-            tma_load_2d(sb + G::kK + st * G::kTile + a * G::kAtom, &kmap, kh * D + a * 64,
-                        s0 + j * 128, bar_k + 8 * st);
+          for (int a = 0; a < D / 64; ++a) {
+            const uint32_t dst = sb + G::kK + st * G::kTile + a * G::kAtom;
+            if (paged) {
+#pragma unroll
+              for (int pp = 0; pp < 8; ++pp)
+                tma_load_2d(dst + pp * 16 * 128, &kmap, a * 64, prow[pp], bar_k + 8 * st);
+            } else {
+              tma_load_2d(dst, &kmap, kh * D + a * 64, s0 + j * 128, bar_k + 8 * st);
+            }
+          }
           ++nk;
           if (nv >= 2 && !mbar_wait_bounded(bar_vfree + 8 * st, ((nv >> 1) - 1) & 1)) {
             ok = false;
@@ -249,9 +290,17 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
           }
           mbar_arrive_expect_tx(bar_v + 8 * st, G::kTile);
 #pragma unroll
-          for (int a = 0; a < D / 64; ++a)
-            tma_load_2d(sb + G::kV + st * G::kTile + a * G::kAtom, &vmap, kh * D + a * 64,
-                        s0 + j * 128, bar_v + 8 * st);
+          for (int a = 0; a < D / 64; ++a) {
+            const uint32_t dst = sb + G::kV + st * G::kTile + a * G::kAtom;
+            if (paged) {
+#pragma unroll
+              for (int pp = 0; pp < 8; ++pp)
+                tma_load_2d(dst + pp * 16 * 128, &kmap, a * 64,
+                            prow[pp] < 0 ? prow[pp] : prow[pp] + v_off, bar_v + 8 * st);
+            } else {
+              tma_load_2d(dst, &vmap, kh * D + a * 64, s0 + j * 128, bar_v + 8 * st);
+            }
+          }
           ++nv;
         }
       }
@@ -295,8 +344,8 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       };
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
         const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
-        int s0, len, nA, nB;
-        if (!extent(w, s0, len, nA, nB)) continue;
+        int s0, len, nA, nB, c;
+        if (!extent(w, s0, len, nA, nB, c)) continue;
         const int n_kv = nB ? nB : nA;
         const int nx[2] = {nA, nB};
         const uint32_t qoff[2] = {(uint32_t)G::kQA, (uint32_t)G::kQB};
@@ -387,11 +436,12 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
     bool ok = true;
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
       const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
-      int s0, len, nA, nB;
-      if (!extent(w, s0, len, nA, nB)) continue;
+      int s0, len, nA, nB, c;
+      if (!extent(w, s0, len, nA, nB, c)) continue;
       const int n_mine = x ? nB : nA;
       if (n_mine == 0) continue;
-      const int qi = pf3_row(w, x, pair) + r;
+      const int qi = pf3_row(w, x, pair) + r;  // row among the new tokens
+      const int qa = c + qi, klen = c + len;     // its key position; keys in total
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_mine; ++j) {
         const bool got = mbar_wait_bounded(bar_s + 8 * x, ns & 1);
@@ -409,12 +459,12 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
         tmem_wait_ld();
         const int kb = j * 128 + hsel * NC;  // key index of this thread's first column
         // whole tile below the diagonal and inside the sequence: no masking
-        const bool full = j * 128 + 127 <= qi && j * 128 + 128 <= len;
+        const bool full = j * 128 + 127 <= qa && j * 128 + 128 <= klen;
         float mxa[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mxa[a] = -INFINITY;
         if (!full) {
-          const int lim = min(qi, len - 1) - kb;  // last visible column of this half
+          const int lim = min(qa, klen - 1) - kb;  // last visible column of this half
 #pragma unroll
           for (int c = 0; c < NCC; ++c)
 #pragma unroll
@@ -580,7 +630,7 @@ inline int pf3_pair_heads(int group) {
 template <typename T, int D, int SPLIT>
 int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                          const int32_t* cu, int B, int hq, int group, int max_seqlen, float sl2,
-                         T* out, int64_t os, cudaStream_t st) {
+                         T* out, int64_t os, cudaStream_t st, const nb::Pf3Paged& pg) {
   using G = nb::Pf3Geom<D>;
   auto kern = nb::prefill_tc3_kernel<T, D, SPLIT>;
   if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc3")) return r2;
@@ -590,7 +640,7 @@ int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUt
   if (units > INT32_MAX) return fail(NB_ERR_UNSUPPORTED, "too many prefill work units");
   const int grid = (int)std::min<int64_t>(units, num_sms());
   kern<<<grid, nb::pf3_threads<SPLIT>(), G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, pair,
-                                                          sl2, out, os);
+                                                          sl2, out, os, pg);
   return check_launch("prefill_tc3");
 }
 
@@ -604,11 +654,33 @@ int launch_prefill_tc3(const void* q, int64_t qs, const void* k, int64_t ks, con
   if (!rc) rc = tensor_map_2d(&km, k, dtype, (uint64_t)hk * D, T_, (uint64_t)ks * 2, 64, 128);
   if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
   if (rc) return rc;
+  const nb::Pf3Paged pg{nullptr, 0, 0, nullptr, 0, 0};
   if (pf3_split() == 2)
     return launch_prefill_tc3_s<T, D, 2>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
-                                         os, st);
+                                         os, st, pg);
   return launch_prefill_tc3_s<T, D, 1>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
-                                       os, st);
+                                       os, st, pg);
+}
+
+// Paged form: q of the new tokens as above; K and V of every key (cached
+// prefix + new tokens) from the cache through the block table.
+template <typename T, int D>
+int launch_prefill_tc3_paged(const void* q, int64_t qs, const void* cache, int nblk, int hk,
+                             int hq, int group, const int32_t* bt, int64_t bts, int maxb,
+                             const int32_t* ctx, const int32_t* cu, int B, int T_, int max_seqlen,
+                             float sl2, void* out, int64_t os, int dtype, cudaStream_t st) {
+  CUtensorMap qm, cm;
+  int rc = tensor_map_2d(&qm, q, dtype, (uint64_t)hq * D, T_, (uint64_t)qs * 2, 64, 128);
+  if (!rc)
+    rc = tensor_map_2d(&cm, cache, dtype, (uint64_t)D, (uint64_t)2 * nblk * hk * 16,
+                       (uint64_t)D * 2, 64, 16);
+  if (rc) return rc;
+  const nb::Pf3Paged pg{bt, bts, maxb, ctx, nblk, hk};
+  if (pf3_split() == 2)
+    return launch_prefill_tc3_s<T, D, 2>(qm, cm, cm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
+                                         os, st, pg);
+  return launch_prefill_tc3_s<T, D, 1>(qm, cm, cm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
+                                       os, st, pg);
 }
 
 }  // namespace nbh

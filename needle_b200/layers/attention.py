@@ -57,6 +57,10 @@ class Attention(nn.Module):
                                         tp_rank=tp_rank)
         self._qkv_w = None
         self._qkv_b = None
+        # False (needle's prefill): the new tokens attend over the new tokens
+        # only; True: over the cached prefix too (ModelRunner's
+        # prefill_with_context), the continuation case needle does not handle
+        self.prefill_with_context = False
 
     @torch.no_grad()
     def fuse_qkv(self) -> None:
@@ -106,7 +110,12 @@ class Attention(nn.Module):
                                    cu_seqlens=cu_seqlens, write_k_back=True)
         else:
             ops.rope_store_kvcache(q, k, v, cos, sin, kv_cache, block_table, context_lens)
-        if is_prefill:
+        if is_prefill and getattr(self, "prefill_with_context", False):
+            # every new token attends over its whole context, cached prefix
+            # included (K/V from the paged cache, just written above)
+            attn = ops.prefill_attention_paged(q, kv_cache, block_table, context_lens,
+                                               cu_seqlens, max_seqlen, self.scale)
+        elif is_prefill:
             attn = ops.prefill_attention(q, k, v, cu_seqlens, max_seqlen, self.scale)
         else:
             plan = ops.decode_plan(T, H, KV, D, block_table.shape[1], kv_cache.shape[3],

@@ -147,7 +147,16 @@ class ModelRunner:
 
     def __init__(self, model_config: ModelConfig, block_size: int = 16, dtype: str = "bfloat16",
                  device: str = "cuda", tensor_parallel_size: int = 1, tp_rank: int = 0,
-                 cuda_graph: bool = True, fuse: bool = True, tp_fused_tokens: int = 1024):
+                 cuda_graph: bool = True, fuse: bool = True, tp_fused_tokens: int = 1024,
+                 prefill_with_context: bool = False):
+        """needle's ModelRunner arguments, plus this library's options:
+        ``cuda_graph`` (decode steps as CUDA graphs), ``fuse`` (one QKV and
+        one gate/up GEMM), ``tp_fused_tokens`` (rows up to which the TP
+        all-reduce runs fused over NVLink), and ``prefill_with_context``: a
+        prefill chunk attends over the sequence's cached prefix too (K/V from
+        the paged cache), the multi-turn / continuation case needle's own
+        prefill does not handle; False keeps needle's behaviour (the new
+        tokens only)."""
         self.model_config = model_config
         self.block_size = block_size
         self.device = torch.device(device)
@@ -169,6 +178,8 @@ class ModelRunner:
         model.eval()
         if fuse:
             model.fuse_projections()
+        for layer in model.model.layers:
+            layer.self_attn.prefill_with_context = prefill_with_context
         self.model = model
         self.sampler = Sampler()
         self.kv_caches: List[torch.Tensor] = []

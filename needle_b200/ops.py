@@ -316,6 +316,36 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return out
 
 
+def prefill_attention_paged(q: torch.Tensor, kv_cache: torch.Tensor, block_table: torch.Tensor,
+                            context_lens: torch.Tensor, cu_seqlens: torch.Tensor,
+                            max_seqlen: int, scale: Optional[float] = None,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal attention of each sequence's new tokens over its whole context
+    (``context_lens[s]`` cached tokens + the new ones), K/V read from the
+    paged cache; the new tokens' K/V must already be in the cache.
+    ``[T, Hq, D]`` out; bf16 / fp16, head_dim 64 or 128."""
+    _cuda(q, kv_cache, block_table, context_lens, cu_seqlens, out)
+    _i32(cu_seqlens, "cu_seqlens")
+    _i32(context_lens, "context_lens")
+    N, kvh, bs, d = _cache_dims(kv_cache)
+    if bs != 16:
+        raise ValueError("paged prefill takes 16-token blocks")
+    bts, maxb = _bt(block_table)
+    T, hq, dq = q.shape
+    if dq != d:
+        raise ValueError(f"q head_dim {dq} != cache head_dim {d}")
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty((T, hq, d), dtype=q.dtype, device=q.device)
+    L.check(L.lib().nb_prefill_attention_paged(
+        q.data_ptr(), _rows(q, "q"), kv_cache.data_ptr(), N, kvh, block_table.data_ptr(), bts, maxb,
+        context_lens.data_ptr(), hq, d, cu_seqlens.data_ptr(), cu_seqlens.shape[0] - 1, T,
+        int(max_seqlen), float(scale), out.data_ptr(), _rows(out, "out"), _dtype(q),
+        _stream(q)))
+    return out
+
+
 # --------------------------------------------------------------------------
 # RMSNorm
 # --------------------------------------------------------------------------

@@ -17,7 +17,8 @@ def test_header_declares_the_hot_path():
                  "nb_last_error", "nb_device_errors", "nb_abi_version", "nb_silu_mul",
                  "nb_swap_kv_blocks", "nb_tp_allreduce_add_rmsnorm", "nb_ipc_handle",
                  "nb_ipc_open", "nb_ipc_close", "nb_paged_decode_noalloc",
-                 "nb_tp_set_wait_limit_ns", "nb_linear", "nb_sample", "nb_slot_mapping"):
+                 "nb_tp_set_wait_limit_ns", "nb_linear", "nb_sample", "nb_slot_mapping",
+                 "nb_prefill_attention_paged"):
         assert name in decl, name
 
 
@@ -204,3 +205,27 @@ def test_linear_arg_checks():
     rc, msg = _err(lib.nb_linear(16, 32, 16, 64, None, 16, 64, 8, 64, 64, L.NB_DTYPE_BF16, None))
     assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
     assert lib.nb_linear(16, 64, 16, 64, None, 16, 64, 0, 64, 64, L.NB_DTYPE_BF16, None) == 0
+
+
+def test_paged_prefill_arg_checks():
+    lib = L.lib()
+    args = dict(q=16, qs=1024, cache=16, nblk=64, kvh=2, bt=16, bts=8, maxb=8, ctx=16, hq=8,
+                d=128, cu=16, B=2, T=10, msl=5, scale=0.1, out=16, os=1024)
+
+    def call(dtype=L.NB_DTYPE_BF16, **kw):
+        a = dict(args, **kw)
+        return _err(lib.nb_prefill_attention_paged(
+            a["q"], a["qs"], a["cache"], a["nblk"], a["kvh"], a["bt"], a["bts"], a["maxb"],
+            a["ctx"], a["hq"], a["d"], a["cu"], a["B"], a["T"], a["msl"], a["scale"], a["out"],
+            a["os"], dtype, None))
+    rc, msg = call(dtype=L.NB_DTYPE_F32)
+    assert rc == L.NB_ERR_UNSUPPORTED
+    rc, msg = call(d=96)
+    assert rc == L.NB_ERR_UNSUPPORTED and "head_dim" in msg
+    rc, msg = call(hq=7)
+    assert rc == L.NB_ERR_INVALID_ARG and "multiple" in msg
+    rc, msg = call(bts=4)
+    assert rc == L.NB_ERR_INVALID_ARG
+    rc, msg = call(qs=512)
+    assert rc == L.NB_ERR_INVALID_ARG and "stride" in msg
+    assert call(T=0)[0] == 0
