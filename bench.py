@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline sample budget (rank 0, N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-ctx", type=int, default=0,
+                    help="prefill workload: cached tokens before each chunk (paged prefill)")
     ap.add_argument("--prefill-shape", default="16x1024",
                     help="prefill workload: sequences x new tokens per sequence")
     ap.add_argument("--workload",
@@ -900,6 +902,7 @@ def run_prefill(args):
     torch.cuda.set_device(dev)
     from needle_b200 import ops
     B, S = (int(v) for v in args.prefill_shape.lower().split("x"))
+    C = args.prefill_ctx  # cached tokens before each chunk (paged prefill)
     H, KV, D = 32, 8, 128
     g = torch.Generator(device=dev).manual_seed(0)
     T = B * S
@@ -908,8 +911,20 @@ def run_prefill(args):
     v = torch.randn(T, KV, D, device=dev, generator=g, dtype=torch.bfloat16)
     cu = torch.arange(0, T + 1, S, dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
+    if C > 0:
+        # the paged form: K/V of C cached + S new tokens per sequence in a
+        # shuffled block pool, read through the block table
+        maxb = (C + S + 15) // 16
+        nblk = B * maxb
+        cache = torch.randn(2, nblk, KV, 16, D, device=dev, generator=g, dtype=torch.bfloat16)
+        bt = torch.randperm(nblk, generator=torch.Generator().manual_seed(0)).view(
+            B, maxb).to(device=dev, dtype=torch.int32)
+        ctx = torch.full((B,), C, dtype=torch.int32, device=dev)
+        call = lambda: ops.prefill_attention_paged(q, cache, bt, ctx, cu, S, out=out)
+    else:
+        call = lambda: ops.prefill_attention(q, k, v, cu, S, out=out)
     for _ in range(max(3, args.warmup)):
-        ops.prefill_attention(q, k, v, cu, S, out=out)
+        call()
     torch.cuda.synchronize(dev)
     st = torch.cuda.current_stream(dev)
     K = args.steps
@@ -919,12 +934,12 @@ def run_prefill(args):
         s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record(st)
         for _ in range(K):
-            ops.prefill_attention(q, k, v, cu, S, out=out)
+            call()
         e0.record(st)
         torch.cuda.synchronize(dev)
         barrier(ws)
     t_ms = max_over_ranks(s0.elapsed_time(e0), ws, dev)
-    flops = B * 4 * (S * (S + 1) / 2) * H * D
+    flops = B * 4 * (S * C + S * (S + 1) / 2) * H * D  # causal QK^T + PV over C + i + 1 keys
     tflops = flops * K / (t_ms / 1e3) / 1e12
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -937,7 +952,9 @@ def run_prefill(args):
             "unit": "TFLOP/s", "n_gpus": ws, "steps": K, "warmup": max(3, args.warmup),
             "ms_per_step": round(t_ms / K, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, N(0,1))",
-            "config": {"workload": f"prefill: {B} x {S} new tokens, 32/8 heads, D=128, causal"},
+            "config": {"workload": f"prefill: {B} x {S} new tokens"
+                                   + (f" after {C} cached (paged K/V)" if C else "")
+                                   + ", 32/8 heads, D=128, causal"},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
                          "peak_source": src, "flops_per_call": flops, "traffic": None},
