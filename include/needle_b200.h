@@ -354,8 +354,10 @@ NB_API int nb_sample(const void* logits, int64_t row_stride, int num_rows, int v
  * continuation case needle's own prefill does not handle (it attends over
  * the new tokens only: needle/layers/attention.py:101-134, and its TODO.md
  * lists the gap); decode attends over the cached tokens the same way
- * (attention.py:291-310), so a chunk of n new tokens equals n decode steps.
- * bf16 / fp16, head_dim 64 or 128, tcgen05; NB_ERR_UNSUPPORTED otherwise.
+ * (attention.py:291-310), so a chunk of n new tokens equals n decode steps;
+ * as in decode, a context longer than max_blocks * 16 keys sees only the
+ * table's pages.  bf16 / fp16, head_dim 64 or 128, tcgen05;
+ * NB_ERR_UNSUPPORTED otherwise.
  */
 NB_API int nb_prefill_attention_paged(const void* q, int64_t q_stride, const void* kv_cache,
                                       int num_blocks, int num_kv_heads, const int32_t* block_table,

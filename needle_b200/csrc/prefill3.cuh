@@ -31,6 +31,8 @@
 // producer waits (bounded) for its copies in flight and the MMA warp for its
 // MMAs, then tensor memory is freed.
 #pragma once
+#include <climits>
+
 #include "nb_common.cuh"
 
 namespace nb {
@@ -207,6 +209,9 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
   const int n_units = nqb * (pair ? hq / 2 : hq) * B;
 
   const bool paged = pg.bt != nullptr;
+  // keys a sequence can have: the block table's pages (as decode, which reads
+  // at most max_blocks pages of a longer context)
+  const int kcap = paged ? pg.maxb * 16 : INT_MAX;
   // Causal extent of a unit: KV tiles under tile A / tile B (0: no tile B);
   // c = the sequence's cached prefix (keys before its new tokens)
   auto extent = [&](const Pf3Unit& w, int& s0, int& len, int& nA, int& nB, int& c) -> bool {
@@ -216,8 +221,9 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
     const int q0 = pf3_row(w, 0, pair);
     if (q0 >= len) return false;
     const int q1 = pf3_row(w, 1, pair);
-    nA = (min(c + q0 + 127, c + len - 1) >> 7) + 1;
-    nB = q1 < len ? (min(c + q1 + 127, c + len - 1) >> 7) + 1 : 0;
+    const int klast = min(c + len, kcap) - 1;  // last key of the sequence
+    nA = (min(c + q0 + 127, klast) >> 7) + 1;
+    nB = q1 < len ? (min(c + q1 + 127, klast) >> 7) + 1 : 0;
     return true;
   };
   // paged mode: first cache row (K half) of page p of sequence b for KV head
@@ -441,7 +447,7 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       const int n_mine = x ? nB : nA;
       if (n_mine == 0) continue;
       const int qi = pf3_row(w, x, pair) + r;  // row among the new tokens
-      const int qa = c + qi, klen = c + len;     // its key position; keys in total
+      const int qa = c + qi, klen = min(c + len, kcap);  // its key position; keys in total
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_mine; ++j) {
         const bool got = mbar_wait_bounded(bar_s + 8 * x, ns & 1);

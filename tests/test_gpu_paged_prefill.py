@@ -99,6 +99,21 @@ def test_paged_prefill_without_context_equals_prefill(cuda):
     assert (a.float() - b.float()).abs().max().item() <= 2e-2
 
 
+def test_paged_prefill_table_narrower_than_context(cuda):
+    """A context longer than the block table reads only its pages, as decode
+    does (needle's block_table[i, :nb] slice): keys past max_blocks * 16 do
+    not exist for either."""
+    ops = _ops()
+    H, kv, D = 8, 2, 128
+    q, cache, bt, cl, cu = _case(H, kv, D, [200, 0], [60, 40], torch.bfloat16, seed=8)
+    bt = bt[:, :12].contiguous()  # 192 keys: shorter than 200 + 60
+    out = ops.prefill_attention_paged(q.to(cuda), cache.to(cuda), bt.to(cuda), cl.to(cuda),
+                                      cu.to(cuda), 60)
+    assert ops.device_errors() == 0
+    ref = _decode_steps_ref(q, cache, bt, cl, cu, H, kv, D)
+    assert (out.float().cpu() - ref.float()).abs().max().item() <= 2e-2
+
+
 def test_paged_prefill_bad_block_id_is_flagged(cuda):
     """A block id outside the pool is recorded and read as zeros, not
     followed."""
