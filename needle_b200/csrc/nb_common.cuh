@@ -390,6 +390,35 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(bool bf16, int M, int N, bo
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Packed fp32 pairs (sm_100): one instruction applies the operation to two
+// values, each rounded exactly as the scalar fma / mul / add rounds it
+// (round to nearest even, denormals kept), so results are bit-identical to
+// the scalar form with half the instructions issued.
+__device__ __forceinline__ void fma_f32x2(float& d0, float& d1, float a0, float a1, float b0,
+                                          float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void mul_f32x2(float& d0, float& d1, float a0, float a1, float b0,
+                                          float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void add_f32x2(float& d0, float& d1, float a0, float a1, float b0,
+                                          float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // 2^x with the hardware approximation instruction (flush-to-zero); used for
 // softmax probabilities, which are rounded to bf16/fp16 right after.
 __device__ __forceinline__ float ex2_approx(float x) {

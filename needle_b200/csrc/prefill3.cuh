@@ -516,7 +516,8 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
           m = mx;
         }
         const float neg_m = -m;
-        float rsa[4] = {0.f, 0.f, 0.f, 0.f};  // row sum in 4 independent partials
+        // row sum in 4 independent partials of (even, odd) column pairs
+        float rsa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
         for (int c = 0; c < NCC; ++c) {
 #pragma unroll
@@ -527,8 +528,9 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
               // masked scores are -inf: the MUFU's exp2 gives exactly 0, so
               // masked tiles use it for every value
               const int i = hh * 16 + 2 * e;
-              const float x0 = fmaf(__uint_as_float(sr[c][i]), scale_log2, neg_m);
-              const float x1 = fmaf(__uint_as_float(sr[c][i + 1]), scale_log2, neg_m);
+              float x0, x1;
+              fma_f32x2(x0, x1, __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
+                        scale_log2, scale_log2, neg_m, neg_m);
               float p0, p1;
               if (e < NB_PF3_POLY && full) {
                 p0 = exp2_poly(x0);
@@ -537,14 +539,16 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
                 p0 = ex2_approx(x0);
                 p1 = ex2_approx(x1);
               }
-              rsa[e & 3] += p0 + p1;
+              add_f32x2(rsa[e & 3][0], rsa[e & 3][1], rsa[e & 3][0], rsa[e & 3][1], p0, p1);
               pk[e] = Mma<T>::pack(p0, p1);
             }
             // P over S's first 64 columns (this half's 32 / 64 of them)
             tmem_st8(tS + lane_off + hsel * (NC / 2) + c * 16 + hh * 8, pk);
           }
         }
-        const float rs = (rsa[0] + rsa[1]) + (rsa[2] + rsa[3]);
+        add_f32x2(rsa[0][0], rsa[0][1], rsa[0][0], rsa[0][1], rsa[1][0], rsa[1][1]);
+        add_f32x2(rsa[2][0], rsa[2][1], rsa[2][0], rsa[2][1], rsa[3][0], rsa[3][1]);
+        const float rs = (rsa[0][0] + rsa[2][0]) + (rsa[0][1] + rsa[2][1]);
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // rescale this thread's O columns (P_X(j-1).V_{j-1} is complete:
           // the commit that signalled S_X(j) covers it; P_X(j).V_j waits for
@@ -554,7 +558,7 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
             float v[32];
             tmem_ld32(tO + lane_off + c * 32, v);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= alpha;
+            for (int i = 0; i < 32; i += 2) mul_f32x2(v[i], v[i + 1], v[i], v[i + 1], alpha, alpha);
             tmem_st32(tO + lane_off + c * 32, v);
           }
         }
@@ -595,8 +599,11 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
           for (int k = 0; k < 4; ++k) {
             uint32_t pk[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              pk[e] = Mma<T>::pack(v[k * 8 + 2 * e] * inv, v[k * 8 + 2 * e + 1] * inv);
+            for (int e = 0; e < 4; ++e) {
+              float a0, a1;
+              mul_f32x2(a0, a1, v[k * 8 + 2 * e], v[k * 8 + 2 * e + 1], inv, inv);
+              pk[e] = Mma<T>::pack(a0, a1);
+            }
             *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) =
                 make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
