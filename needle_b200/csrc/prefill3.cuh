@@ -12,18 +12,23 @@
 //     tiles first (the last query blocks of the longest sequences), so the
 //     causal triangle's long units start early and short ones fill the tail.
 //     Tensor memory is allocated once per CTA, not once per unit.
-//   * Ten warps: warp 0 issues TMA loads, warp 1 issues the MMAs (one lane),
-//     warps 2-5 and 6-9 run the softmax of tiles A and B (thread = query row
-//     = TMEM lane; warp w reaches lanes 32 (w mod 4) .. +31) and the epilogue.  K and V have separate two-stage rings
+//   * Sixteen warps in four warpgroups: warps 0-3 and 4-7 run the softmax of
+//     tiles A and B (thread = query row = TMEM lane; warp w reaches lanes
+//     32 (w mod 4) .. +31), warps 8-11 write out O (the epilogue), warp 12
+//     issues TMA loads, warp 13 issues the MMAs (one lane), warps 14-15 only
+//     take part in the register split.  `setmaxnreg` moves registers from the
+//     epilogue and issuing warpgroups to the softmax warpgroups, which hold a
+//     row's 128 scores in registers.  K and V have separate two-stage rings
 //     with their own "free" barriers: K_j is released as soon as both S MMAs
 //     that read it finish, V_j after both P.V MMAs.
 //   * A softmax thread loads its 128 scores from tensor memory with four
 //     loads and one wait, keeps them in registers for the max and the
 //     exponentials, and stores P back with four stores and one wait.
 //   * The next unit's Q tiles load as soon as the current unit's last S MMA
-//     has finished, and its first S MMAs run while the softmax warps write
-//     out the current unit's O (tensor memory O is handed back to the MMA warp
-//     through an "O free" barrier after the epilogue read it).
+//     has finished; its first S MMAs and softmax run while the epilogue
+//     warps read out the current unit's O (the row sums reach them through
+//     shared memory, double-buffered by unit; tensor memory O is handed back
+//     to the MMA warp through an "O free" barrier once read).
 //
 // Every wait is bounded (kWaitLimitNs).  A role that gives up sets an abort
 // flag in shared memory and records NB_DEVERR_TIMEOUT; every role checks the
@@ -60,10 +65,6 @@ __device__ __forceinline__ float exp2_poly(float x) {
 #ifndef NB_PF3_POLY
 #define NB_PF3_POLY 0
 #endif
-// threads per query row in the softmax groups (1 or 2)
-#ifndef NB_PF3_SPLIT_DEFAULT
-#define NB_PF3_SPLIT_DEFAULT 1
-#endif
 
 template <int D> struct Pf3Geom {
   static constexpr int kAtom = 128 * 128;       // 128 rows x 128 B
@@ -73,29 +74,34 @@ template <int D> struct Pf3Geom {
   static constexpr int kK = 2 * kTile;          // K ring: 2 stages
   static constexpr int kV = kK + 2 * kTile;     // V ring: 2 stages
   static constexpr int kBars = kV + 2 * kTile;
-  // row-max exchange [group][parity][half][row] and row-sum exchange
-  // [group][half][row] between the two warps that share a row (SPLIT = 2)
-  static constexpr int kXchg = kBars + 256;
-  static constexpr int kSmem = kXchg + (2 * 2 * 2 * 128 + 2 * 2 * 128) * 4 + 1024;
+  // row sums handed from the softmax groups to the epilogue:
+  // [group][unit parity][row] floats
+  static constexpr int kRowSum = kBars + 256;
+  static constexpr int kSmem = kRowSum + 2 * 2 * 128 * 4 + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kSA = 0, kSB = 128, kOA = 256, kOB = 256 + D;
 };
-template <int SPLIT> constexpr int pf3_threads() { return 64 + 256 * SPLIT; }
+// Warp roles (four warpgroups; a warp reaches the TMEM lanes 32 (w mod 4) ..
+// +31) and the register split between them.  The block is launched with
+// kPf3Threads x kPf3LaunchRegs registers (the whole register file); the
+// shares after `setmaxnreg` add up to exactly that (checked below and, on
+// the host, against the compiled kernel before the first launch).
+constexpr int kPf3Threads = 512;
+constexpr int kPf3LaunchRegs = 128;
+constexpr int kPf3SoftmaxRegs = 168;   // warpgroups 0, 1
+constexpr int kPf3EpilogueRegs = 72;   // warpgroup 2
+constexpr int kPf3IssueRegs = 104;     // warpgroup 3 (TMA, MMA, two idle warps)
+static_assert(128 * (2 * kPf3SoftmaxRegs + kPf3EpilogueRegs + kPf3IssueRegs) <=
+                  kPf3Threads * kPf3LaunchRegs,
+              "the register split must fit the registers the block is launched with");
+static_assert(kPf3Threads * kPf3LaunchRegs <= 65536, "one CTA per SM");
+constexpr int kPf3WarpEpi = 8, kPf3WarpTma = 12, kPf3WarpMma = 13;
 
-// Named barrier of one softmax group (id 1 + group) that also ORs a
-// predicate over its threads: every thread of the group gets the same answer
-// (a group leaves its loops together, so no thread is left at a barrier).
-__device__ __forceinline__ bool group_bar_or(int id, int nthreads, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "barrier.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
-      : "memory");
-  return r != 0;
+template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N> __device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // max(a, b, c) in one instruction (sm_100 three-input max; NaN handling as
@@ -144,11 +150,8 @@ __device__ __forceinline__ int pf3_head(const Pf3Unit& w, int x, int pair) {
   return pair ? w.h + x : w.h;
 }
 
-// SPLIT = 1: one softmax thread per query row (warps 2-9);
-// SPLIT = 2: two threads per row, one per half of the 128 scores (warps 2-17),
-// which halves the serial softmax work per tile.
-template <typename T, int D, int SPLIT>
-__global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
+template <typename T, int D>
+__global__ void __launch_bounds__(kPf3Threads, 1)
     prefill_tc3_kernel(const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
@@ -175,14 +178,16 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
   const uint32_t bar_o = bar_q + 112;              // [2] O_A / O_B final
   const uint32_t bar_ofree = bar_q + 128;          // [2] O_A / O_B read out (128 arrivals)
   const uint32_t bar_end = bar_q + 144;            // every MMA of the CTA finished
+  const uint32_t bar_l = bar_q + 152;              // [group][unit parity] row sums written
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G::kBars + 192);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kBars + 200);
+  float* rowsum = reinterpret_cast<float*>(smem + G::kRowSum);  // [2][2][128]
 
-  if (warp == 1) {
+  if (warp == kPf3WarpMma) {
     tmem_alloc(smem_u32(tmem_slot), G::kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == kPf3WarpTma && lane == 0) {
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
@@ -193,10 +198,11 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       mbar_init(bar_kfree + 8 * i, 1);
       mbar_init(bar_vfree + 8 * i, 1);
       mbar_init(bar_s + 8 * i, 1);
-      mbar_init(bar_p + 8 * i, 128 * SPLIT);
+      mbar_init(bar_p + 8 * i, 128);
       mbar_init(bar_o + 8 * i, 1);
-      mbar_init(bar_ofree + 8 * i, 128 * SPLIT);
+      mbar_init(bar_ofree + 8 * i, 128);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(bar_l + 8 * i, 128);
     mbar_init(bar_qfree, 1);
     mbar_init(bar_end, 1);
     *abort_flag = 0;
@@ -247,7 +253,10 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
     return (phys * pg.kvh + kh) * 16;
   };
 
-  if (warp == 0) {
+  const int wg = warp >> 2;
+  if (wg == 3) {
+    setmaxnreg_dec<kPf3IssueRegs>();
+  if (warp == kPf3WarpTma) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t nq = 0, nk = 0, nv = 0;  // loads issued (running counts)
@@ -330,7 +339,7 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       for (uint32_t i = (nv > 2 ? nv - 2 : 0); i < nv; ++i)
         mbar_wait_bounded(bar_v + 8 * (i & 1), (i >> 1) & 1);
     }
-  } else if (warp == 1) {
+  } else if (warp == kPf3WarpMma) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t nq = 0, nk = 0, nv = 0;           // tiles consumed (running counts)
@@ -356,18 +365,30 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
                         smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
                         (!first || kk > 0) ? 1u : 0u);
       };
-      for (int rd = 0, u = unit_of(0); ok && u < n_units; u = unit_of(++rd)) {
-        const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
-        int s0, len, nA, nB, c;
-        if (!extent(w, s0, len, nA, nB, c)) continue;
+      // the first unit at or after round rd with work (its KV tile counts)
+      auto next_unit = [&](int& rd, int& tA, int& tB) -> bool {
+        for (int u = unit_of(rd); u < n_units; u = unit_of(++rd)) {
+          int s0, len, c;
+          if (extent(pf3_unit(u, hq, B, nqb, pair), s0, len, tA, tB, c)) return true;
+        }
+        return false;
+      };
+      const uint32_t qoff[2] = {(uint32_t)G::kQA, (uint32_t)G::kQB};
+      const uint32_t scol[2] = {G::kSA, G::kSB}, ocol[2] = {G::kOA, G::kOB};
+      int rd = 0, nA = 0, nB = 0;
+      bool have = next_unit(rd, nA, nB);
+      bool first_unit = true;
+      while (ok && have) {
         const int n_kv = nB ? nB : nA;
         const int nx[2] = {nA, nB};
-        const uint32_t qoff[2] = {(uint32_t)G::kQA, (uint32_t)G::kQB};
-        const uint32_t scol[2] = {G::kSA, G::kSB}, ocol[2] = {G::kOA, G::kOB};
-        if (!wait(bar_q, nq & 1)) break;
-        ++nq;
-        // S_X(0) for both tiles
-        {
+        int rd2 = rd + 1, mA = 0, mB = 0;
+        const bool have2 = next_unit(rd2, mA, mB);
+        const int mx[2] = {mA, mB};
+        if (first_unit) {
+          // S_X(0) for both tiles (later units' are issued at the end of the
+          // unit before them)
+          if (!wait(bar_q, nq & 1)) break;
+          ++nq;
           const uint32_t st = nk & 1;
           if (!wait(bar_k + 8 * st, (nk >> 1) & 1)) break;
           tc_fence_after();
@@ -380,7 +401,23 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
           tc_commit(bar_kfree + 8 * st);
           if (n_kv == 1) tc_commit(bar_qfree);
           ++nk;
+          first_unit = false;
         }
+        // the next unit's Q / K_0 landed (waited), its S_X(0) issued (bit x)
+        bool q2 = false, k2 = false;
+        uint32_t early = 0;
+        auto next_ready = [&]() -> bool {
+          if (!q2) {
+            if (!wait(bar_q, nq & 1)) return false;
+            q2 = true;
+          }
+          if (!k2) {
+            if (!wait(bar_k + 8 * (nk & 1), (nk >> 1) & 1)) return false;
+            tc_fence_after();
+            k2 = true;
+          }
+          return true;
+        };
         for (int j = 0; ok && j < n_kv; ++j) {
           const uint32_t vst = nv & 1;
           if (!wait(bar_v + 8 * vst, (nv >> 1) & 1)) break;
@@ -400,6 +437,17 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
             if (j + 1 == nx[x]) {
               tc_commit(bar_o + 8 * x);  // O_X final for this unit
               ++no[x];
+              // At the unit's last KV tile the next unit's S_X(0) goes in
+              // right behind this P.V, before the other tile's P is waited
+              // for: its Q was requested when this unit's last S MMAs were
+              // issued and its K_0 when the stage before it was freed, so the
+              // producer needs nothing more from this warp.
+              if (have2 && mx[x] && !has_next) {
+                if (!next_ready()) break;
+                issue_s(qoff[x], sb + G::kK + (nk & 1) * G::kTile, scol[x]);
+                tc_commit(bar_s + 8 * x);  // also covers P_X(j).V_j
+                early |= 1u << x;
+              }
             } else {
               if (!k_ready) {
                 if (!wait(bar_k + 8 * kst, (nk >> 1) & 1)) break;
@@ -419,6 +467,26 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
             ++nk;
           }
         }
+        if (!ok) break;
+        if (have2) {
+          // the next unit's remaining S_X(0) (a tile that ended before this
+          // unit's last KV tile), then its Q and K_0 bookkeeping
+          if (!next_ready()) break;
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (!mx[x] || ((early >> x) & 1u)) continue;
+            issue_s(qoff[x], sb + G::kK + (nk & 1) * G::kTile, scol[x]);
+            tc_commit(bar_s + 8 * x);
+          }
+          ++nq;
+          tc_commit(bar_kfree + 8 * (nk & 1));
+          if ((mB ? mB : mA) == 1) tc_commit(bar_qfree);
+          ++nk;
+        }
+        rd = rd2;
+        nA = mA;
+        nB = mB;
+        have = have2;
       }
       if (!ok) {
         *abort_flag = 1;
@@ -427,25 +495,20 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       tc_commit(bar_end);
       mbar_wait_bounded(bar_end, 0);  // every MMA issued by this CTA has finished
     }
-  } else {
-    // ---------------- softmax groups + epilogue ----------------
-    constexpr int NC = 128 / SPLIT;        // score columns per thread
-    constexpr int NCC = NC / 32;           // 32-column TMEM chunks per thread
-    constexpr int OC = D / 32 / SPLIT;     // O chunks per thread
-    const int sw = warp - 2;
-    const int x = sw / (4 * SPLIT);        // 0 = tile A, 1 = tile B
-    const int hsel = (sw >> 2) % SPLIT;    // which half of the row (SPLIT = 2)
+  }
+  } else if (wg < 2) {
+    setmaxnreg_inc<kPf3SoftmaxRegs>();
+    // ---------------- softmax groups ----------------
+    constexpr int NCC = 4;                 // 32-column TMEM chunks of a row's 128 scores
+    constexpr int OC = D / 32;             // 32-column O chunks
+    const int x = wg;                      // 0 = tile A, 1 = tile B
     // A warp reaches the TMEM lanes of its warp index mod 4: lanes [32 wq,
-    // 32 wq + 32).  Each set of four warps is quarters 2, 3, 0, 1: it covers
-    // all 128 lanes, and a thread's query row is its TMEM lane.
+    // 32 wq + 32); a thread's query row is its TMEM lane.
     const int wq = warp & 3;
     const uint32_t tS = tmem + (x ? G::kSB : G::kSA);
-    const uint32_t tO = tmem + (x ? G::kOB : G::kOA) + hsel * (D / SPLIT);
+    const uint32_t tO = tmem + (x ? G::kOB : G::kOA);
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const int r = wq * 32 + lane;
-    float* xmax = reinterpret_cast<float*>(smem + G::kXchg);   // [2][2][2][128]
-    float* xsum = xmax + 2 * 2 * 2 * 128;                      // [2][2][128]
-    const int gbar = 1 + x, gthreads = 128 * SPLIT;
     uint32_t ns = 0, nunits = 0;
     bool ok = true;
     for (int rd = 0, u = unit_of(0); ok && u < n_units; u = unit_of(++rd)) {
@@ -459,9 +522,8 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_mine; ++j) {
         const bool got = mbar_wait_bounded(bar_s + 8 * x, ns & 1);
-        const int par = ns & 1;
         ++ns;
-        if (SPLIT == 1 && (__any_sync(0xffffffffu, !got) || *abort_flag)) {
+        if (__any_sync(0xffffffffu, !got) || *abort_flag) {
           ok = false;
           break;
         }
@@ -469,16 +531,16 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
         uint32_t sr[NCC][32];
 #pragma unroll
         for (int c = 0; c < NCC; ++c)
-          tmem_ld32_nowait(tS + lane_off + hsel * NC + c * 32, sr[c]);
+          tmem_ld32_nowait(tS + lane_off + c * 32, sr[c]);
         tmem_wait_ld();
-        const int kb = j * 128 + hsel * NC;  // key index of this thread's first column
+        const int kb = j * 128;  // key index of the tile's first column
         // whole tile below the diagonal and inside the sequence: no masking
         const bool full = j * 128 + 127 <= qa && j * 128 + 128 <= klen;
         float mxa[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mxa[a] = -INFINITY;
         if (!full) {
-          const int lim = min(qa, klen - 1) - kb;  // last visible column of this half
+          const int lim = min(qa, klen - 1) - kb;  // last visible column of the row
 #pragma unroll
           for (int c = 0; c < NCC; ++c)
 #pragma unroll
@@ -493,21 +555,6 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
                                       __uint_as_float(sr[c][i + 1]));
         float mx = fmax3(fmax3(mxa[0], mxa[1], mxa[2]), fmax3(mxa[3], mxa[4], mxa[5]),
                          fmaxf(mxa[6], mxa[7]));
-        if constexpr (SPLIT == 2) {
-          // both halves of the row publish their maximum (double-buffered by
-          // tile parity); the barrier also tells the whole group whether any
-          // thread's wait gave up
-          xmax[((x * 2 + par) * 2 + hsel) * 128 + r] = mx;
-          // the barrier also orders this thread's completed S loads before
-          // the partner's P stores into the same TMEM columns
-          tc_fence_before();
-          if (group_bar_or(gbar, gthreads, !got || *abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          mx = fmaxf(mx, xmax[((x * 2 + par) * 2 + (hsel ^ 1)) * 128 + r]);
-        }
         mx *= scale_log2;  // scale > 0: max of scaled scores = scaled max
         const bool need = mx > m + kRescaleThreshold;
         float alpha = 1.f;
@@ -542,8 +589,8 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
               add_f32x2(rsa[e & 3][0], rsa[e & 3][1], rsa[e & 3][0], rsa[e & 3][1], p0, p1);
               pk[e] = Mma<T>::pack(p0, p1);
             }
-            // P over S's first 64 columns (this half's 32 / 64 of them)
-            tmem_st8(tS + lane_off + hsel * (NC / 2) + c * 16 + hh * 8, pk);
+            // P over S's first 64 columns
+            tmem_st8(tS + lane_off + c * 16 + hh * 8, pk);
           }
         }
         add_f32x2(rsa[0][0], rsa[0][1], rsa[0][0], rsa[0][1], rsa[1][0], rsa[1][1]);
@@ -563,55 +610,77 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
           }
         }
         tmem_wait_st();
-        l = l * alpha + rs;  // this thread's share of the row sum
+        l = l * alpha + rs;
         tc_fence_before();
         mbar_arrive(bar_p + 8 * x);
       }
       if (!ok) break;
-      // epilogue: O_X / l -> out rows
-      const bool done = mbar_wait_bounded(bar_o + 8 * x, nunits & 1);
-      if constexpr (SPLIT == 1) {
+      // the row sum to the epilogue warps (double-buffered by unit: the
+      // group can finish the next unit before the epilogue read this one)
+      const uint32_t up = nunits & 1;
+      rowsum[(2 * x + up) * 128 + r] = l;
+      mbar_arrive(bar_l + 8 * (2 * x + up));
+      ++nunits;
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      if (lane == 0) set_error(kErrTimeout);
+    }
+  } else {
+    setmaxnreg_dec<kPf3EpilogueRegs>();
+    // ---------------- epilogue: O_X / l -> out rows ----------------
+    constexpr int OC = D / 32;  // 32-column O chunks
+    const int wq = warp & 3;    // TMEM lane quarter, as in the softmax groups
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const int r = wq * 32 + lane;
+    uint32_t ne[2] = {0, 0};    // units written out per tile
+    bool ok = true;
+    for (int rd = 0, u = unit_of(0); ok && u < n_units; u = unit_of(++rd)) {
+      const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
+      int s0, len, nA, nB, c;
+      if (!extent(w, s0, len, nA, nB, c)) continue;
+      const int nx[2] = {nA, nB};
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        if (!nx[x]) continue;
+        const uint32_t e = ne[x]++;
+        const uint32_t lb = 2 * x + (e & 1);
+        // O_X final (the MMA warp's commit after the unit's last P.V) and
+        // the group's row sums written
+        const bool done = mbar_wait_bounded(bar_o + 8 * x, e & 1) &&
+                          mbar_wait_bounded(bar_l + 8 * lb, (e >> 1) & 1);
         if (__any_sync(0xffffffffu, !done) || *abort_flag) {
           ok = false;
           break;
         }
-      } else {
-        xsum[(x * 2 + hsel) * 128 + r] = l;
-        if (group_bar_or(gbar, gthreads, !done || *abort_flag)) {
-          ok = false;
-          break;
-        }
-        // the same order of the two partial sums in both halves
-        l = xsum[(x * 2 + 0) * 128 + r] + xsum[(x * 2 + 1) * 128 + r];
-      }
-      tc_fence_after();
-      const float inv = 1.f / l;
-      T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)pf3_head(w, x, pair) * D +
-               hsel * (D / SPLIT);
-      // one 32-column chunk at a time: load, convert, store; O_X handed back
-      // after the last chunk
+        tc_fence_after();
+        const float inv = 1.f / rowsum[lb * 128 + r];
+        const int qi = pf3_row(w, x, pair) + r;  // row among the new tokens
+        T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)pf3_head(w, x, pair) * D;
+        const uint32_t tO = tmem + (x ? G::kOB : G::kOA);
+        // one 32-column chunk at a time: load, normalise, convert, store
 #pragma unroll 1
-      for (int c = 0; c < OC; ++c) {
-        float v[32];
-        tmem_ld32(tO + lane_off + c * 32, v);
-        if (qi < len) {
+        for (int cc = 0; cc < OC; ++cc) {
+          float v[32];
+          tmem_ld32(tO + lane_off + cc * 32, v);
+          if (qi < len) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            uint32_t pk[4];
+            for (int k = 0; k < 4; ++k) {
+              uint32_t pk[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float a0, a1;
-              mul_f32x2(a0, a1, v[k * 8 + 2 * e], v[k * 8 + 2 * e + 1], inv, inv);
-              pk[e] = Mma<T>::pack(a0, a1);
+              for (int h = 0; h < 4; ++h) {
+                float a0, a1;
+                mul_f32x2(a0, a1, v[k * 8 + 2 * h], v[k * 8 + 2 * h + 1], inv, inv);
+                pk[h] = Mma<T>::pack(a0, a1);
+              }
+              *reinterpret_cast<uint4*>(dst + cc * 32 + k * 8) =
+                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            *reinterpret_cast<uint4*>(dst + c * 32 + k * 8) =
-                make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         }
+        tc_fence_before();
+        mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
       }
-      tc_fence_before();
-      mbar_arrive(bar_ofree + 8 * x);  // the MMA warp may overwrite O_X
-      ++nunits;
     }
     if (!ok) {
       *abort_flag = 1;
@@ -620,7 +689,7 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kPf3WarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, G::kTmemCols);
   }
@@ -629,14 +698,6 @@ __global__ void __launch_bounds__(pf3_threads<SPLIT>(), 1)
 }  // namespace nb
 
 namespace nbh {
-
-inline int pf3_split() {
-  static int v = [] {
-    const char* e = getenv("NB_PF3_SPLIT");  // "1" / "2": threads per query row (diagnostics)
-    return (e && e[0] == '1') ? 1 : (e && e[0] == '2') ? 2 : NB_PF3_SPLIT_DEFAULT;
-  }();
-  return v;
-}
 
 // Head pairs for even GQA groups (NB_PF3_PAIR=0 keeps the row halves of one
 // head; diagnostics).
@@ -648,20 +709,44 @@ inline int pf3_pair_heads(int group) {
   return (on && group % 2 == 0) ? 1 : 0;
 }
 
-template <typename T, int D, int SPLIT>
+// The kernel's warpgroups re-divide the registers the block is launched
+// with (setmaxnreg); a block launched with fewer than the split adds up to
+// would leave the softmax warps waiting for registers, so the compiled
+// kernel's per-thread count is checked once per instantiation before its
+// first launch.
+template <typename T, int D>
+int pf3_check_registers() {
+  static const int rc = [] {
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, (const void*)nb::prefill_tc3_kernel<T, D>) != cudaSuccess)
+      return fail(NB_ERR_CUDA, "prefill_tc3: cudaFuncGetAttributes failed");
+    const long have = (long)a.numRegs * nb::kPf3Threads;
+    const long need = 128L * (2 * nb::kPf3SoftmaxRegs + nb::kPf3EpilogueRegs + nb::kPf3IssueRegs);
+    if (a.numRegs != nb::kPf3LaunchRegs || have < need)
+      return fail(NB_ERR_UNSUPPORTED,
+                  "prefill_tc3: compiled with %d registers per thread, the register split "
+                  "needs %d",
+                  a.numRegs, nb::kPf3LaunchRegs);
+    return 0;
+  }();
+  return rc;
+}
+
+template <typename T, int D>
 int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                          const int32_t* cu, int B, int hq, int group, int max_seqlen, float sl2,
                          T* out, int64_t os, cudaStream_t st, const nb::Pf3Paged& pg) {
   using G = nb::Pf3Geom<D>;
-  auto kern = nb::prefill_tc3_kernel<T, D, SPLIT>;
+  auto kern = nb::prefill_tc3_kernel<T, D>;
+  if (int r1 = pf3_check_registers<T, D>()) return r1;
   if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc3")) return r2;
   const int pair = pf3_pair_heads(group);
   const int nqb = pair ? (max_seqlen + 127) / 128 : (max_seqlen + 255) / 256;
   const int64_t units = (int64_t)nqb * (pair ? hq / 2 : hq) * B;
   if (units > INT32_MAX) return fail(NB_ERR_UNSUPPORTED, "too many prefill work units");
   const int grid = (int)std::min<int64_t>(units, num_sms());
-  kern<<<grid, nb::pf3_threads<SPLIT>(), G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, pair,
-                                                          sl2, out, os, pg);
+  kern<<<grid, nb::kPf3Threads, G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, pair, sl2, out,
+                                                 os, pg);
   return check_launch("prefill_tc3");
 }
 
@@ -676,11 +761,8 @@ int launch_prefill_tc3(const void* q, int64_t qs, const void* k, int64_t ks, con
   if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
   if (rc) return rc;
   const nb::Pf3Paged pg{nullptr, 0, 0, nullptr, 0, 0};
-  if (pf3_split() == 2)
-    return launch_prefill_tc3_s<T, D, 2>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
-                                         os, st, pg);
-  return launch_prefill_tc3_s<T, D, 1>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
-                                       os, st, pg);
+  return launch_prefill_tc3_s<T, D>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out, os, st,
+                                    pg);
 }
 
 // Paged form: q of the new tokens as above; K and V of every key (cached
@@ -697,11 +779,8 @@ int launch_prefill_tc3_paged(const void* q, int64_t qs, const void* cache, int n
                        (uint64_t)D * 2, 64, 16);
   if (rc) return rc;
   const nb::Pf3Paged pg{bt, bts, maxb, ctx, nblk, hk};
-  if (pf3_split() == 2)
-    return launch_prefill_tc3_s<T, D, 2>(qm, cm, cm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
-                                         os, st, pg);
-  return launch_prefill_tc3_s<T, D, 1>(qm, cm, cm, cu, B, hq, group, max_seqlen, sl2, (T*)out,
-                                       os, st, pg);
+  return launch_prefill_tc3_s<T, D>(qm, cm, cm, cu, B, hq, group, max_seqlen, sl2, (T*)out, os, st,
+                                    pg);
 }
 
 }  // namespace nbh
