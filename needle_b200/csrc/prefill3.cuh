@@ -77,7 +77,10 @@ template <int D> struct Pf3Geom {
   // row sums handed from the softmax groups to the epilogue:
   // [group][unit parity][row] floats
   static constexpr int kRowSum = kBars + 256;
-  static constexpr int kSmem = kRowSum + 2 * 2 * 128 * 4 + 1024;
+  // the epilogue's staging box for a TMA store of O: 128 rows x 64 columns,
+  // 128-byte swizzle (1024-byte aligned)
+  static constexpr int kOStage = kRowSum + 3072 - 256;
+  static constexpr int kSmem = kOStage + kAtom + 1024;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kSA = 0, kSB = 128, kOA = 256, kOB = 256 + D;
 };
@@ -156,8 +159,11 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
                        const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, const int32_t* __restrict__ cu,
                        int B, int hq, int group, int nqb, int pair, float scale_log2,
-                       T* __restrict__ out, int64_t os, const Pf3Paged pg) {
+                       T* __restrict__ out, int64_t os, const Pf3Paged pg,
+                       const __grid_constant__ CUtensorMap omap, int o_tma) {
   using G = Pf3Geom<D>;
+  static_assert(G::kOStage % 1024 == 0 && G::kOStage >= G::kRowSum + 2 * 2 * 128 * 4,
+                "staging box placement");
   constexpr bool kBf16 = !__is_same(T, __half);
   constexpr uint32_t kIdS = idesc_f16_f32(kBf16, 128, 128, false, false);
   constexpr uint32_t kIdO = idesc_f16_f32(kBf16, 128, D, false, true);
@@ -649,15 +655,59 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
         // the group's row sums written
         const bool done = mbar_wait_bounded(bar_o + 8 * x, e & 1) &&
                           mbar_wait_bounded(bar_l + 8 * lb, (e >> 1) & 1);
-        if (__any_sync(0xffffffffu, !done) || *abort_flag) {
+        // one answer for all four epilogue warps (they share named barriers)
+        if (named_bar_or(1, 128, !done || *abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const float inv = 1.f / rowsum[lb * 128 + r];
-        const int qi = pf3_row(w, x, pair) + r;  // row among the new tokens
-        T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)pf3_head(w, x, pair) * D;
+        const int q0 = pf3_row(w, x, pair);
+        const int qi = q0 + r;  // row among the new tokens
         const uint32_t tO = tmem + (x ? G::kOB : G::kOA);
+        if (o_tma && q0 + 128 <= len) {
+          // a whole tile inside the sequence: 64-column boxes staged in
+          // shared memory (128-byte swizzle: 16-byte chunk k of row r at
+          // k ^ (r mod 8)) and written by one TMA store each
+          const uint32_t stage = sb + G::kOStage + r * 128;
+#pragma unroll 1
+          for (int hb = 0; hb < D / 64; ++hb) {
+            // the box is free once the previous store has read it
+            if (warp == kPf3WarpEpi && lane == 0) bulk_wait_read_all();
+            named_bar_sync(1, 128);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              float v[32];
+              tmem_ld32(tO + lane_off + (hb * 2 + half) * 32, v);
+              if (hb * 2 + half + 1 == OC) {
+                tc_fence_before();
+                mbar_arrive(bar_ofree + 8 * x);  // O_X read out: the MMA warp may overwrite it
+              }
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  float a0, a1;
+                  mul_f32x2(a0, a1, v[k * 8 + 2 * h], v[k * 8 + 2 * h + 1], inv, inv);
+                  pk[h] = Mma<T>::pack(a0, a1);
+                }
+                const uint32_t chunk = (uint32_t)((half * 4 + k) ^ (r & 7));
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stage + chunk * 16),
+                             "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
+                             : "memory");
+              }
+            }
+            fence_proxy_async_smem();
+            named_bar_sync(1, 128);
+            if (warp == kPf3WarpEpi && lane == 0) {
+              tma_store_2d(&omap, sb + G::kOStage, pf3_head(w, x, pair) * D + hb * 64, s0 + q0);
+              bulk_commit_group();
+            }
+          }
+          continue;
+        }
+        T* dst = out + (int64_t)(s0 + qi) * os + (int64_t)pf3_head(w, x, pair) * D;
         // one 32-column chunk at a time: load, normalise, convert, store
 #pragma unroll 1
         for (int cc = 0; cc < OC; ++cc) {
@@ -686,6 +736,8 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
       *abort_flag = 1;
       if (lane == 0) set_error(kErrTimeout);
     }
+    // the staged boxes are written out before the CTA exits
+    if (warp == kPf3WarpEpi && lane == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -732,11 +784,34 @@ int pf3_check_registers() {
   return rc;
 }
 
+// Whole 128-row output tiles go out through shared memory and TMA stores
+// (NB_PF3_TMA_STORE=0: every row by plain 16-byte stores; diagnostics).
+inline bool pf3_tma_store_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NB_PF3_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <typename T, int D>
 int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
-                         const int32_t* cu, int B, int hq, int group, int max_seqlen, float sl2,
-                         T* out, int64_t os, cudaStream_t st, const nb::Pf3Paged& pg) {
+                         const int32_t* cu, int B, int T_, int hq, int group, int max_seqlen,
+                         float sl2, T* out, int64_t os, int dtype, cudaStream_t st,
+                         const nb::Pf3Paged& pg) {
   using G = nb::Pf3Geom<D>;
+  // the output map (16-byte aligned base and row pitch; otherwise, or when
+  // disabled, plain stores and any valid map in its place)
+  CUtensorMap om = qm;
+  int o_tma = 0;
+  if (pf3_tma_store_enabled() && T_ > 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+      ((uint64_t)os * sizeof(T)) % 16 == 0) {
+    if (tensor_map_2d(&om, out, dtype, (uint64_t)hq * D, (uint64_t)T_, (uint64_t)os * sizeof(T),
+                      64, 128) == NB_OK)
+      o_tma = 1;
+    else
+      om = qm;
+  }
   auto kern = nb::prefill_tc3_kernel<T, D>;
   if (int r1 = pf3_check_registers<T, D>()) return r1;
   if (int r2 = ensure_max_smem((const void*)kern, G::kSmem, "prefill_tc3")) return r2;
@@ -746,7 +821,7 @@ int launch_prefill_tc3_s(const CUtensorMap& qm, const CUtensorMap& km, const CUt
   if (units > INT32_MAX) return fail(NB_ERR_UNSUPPORTED, "too many prefill work units");
   const int grid = (int)std::min<int64_t>(units, num_sms());
   kern<<<grid, nb::kPf3Threads, G::kSmem, st>>>(qm, km, vm, cu, B, hq, group, nqb, pair, sl2, out,
-                                                 os, pg);
+                                                 os, pg, om, o_tma);
   return check_launch("prefill_tc3");
 }
 
@@ -761,8 +836,8 @@ int launch_prefill_tc3(const void* q, int64_t qs, const void* k, int64_t ks, con
   if (!rc) rc = tensor_map_2d(&vm, v, dtype, (uint64_t)hk * D, T_, (uint64_t)vs * 2, 64, 128);
   if (rc) return rc;
   const nb::Pf3Paged pg{nullptr, 0, 0, nullptr, 0, 0};
-  return launch_prefill_tc3_s<T, D>(qm, km, vm, cu, B, hq, group, max_seqlen, sl2, (T*)out, os, st,
-                                    pg);
+  return launch_prefill_tc3_s<T, D>(qm, km, vm, cu, B, T_, hq, group, max_seqlen, sl2, (T*)out, os,
+                                    dtype, st, pg);
 }
 
 // Paged form: q of the new tokens as above; K and V of every key (cached
@@ -779,8 +854,8 @@ int launch_prefill_tc3_paged(const void* q, int64_t qs, const void* cache, int n
                        (uint64_t)D * 2, 64, 16);
   if (rc) return rc;
   const nb::Pf3Paged pg{bt, bts, maxb, ctx, nblk, hk};
-  return launch_prefill_tc3_s<T, D>(qm, cm, cm, cu, B, hq, group, max_seqlen, sl2, (T*)out, os, st,
-                                    pg);
+  return launch_prefill_tc3_s<T, D>(qm, cm, cm, cu, B, T_, hq, group, max_seqlen, sl2, (T*)out, os,
+                                    dtype, st, pg);
 }
 
 }  // namespace nbh

@@ -516,6 +516,34 @@ def test_prefill_many_units_per_cta(cuda, lens):
     assert err <= 2e-2, err
 
 
+def test_prefill_output_store_paths_agree(cuda):
+    """Whole 128-row output tiles leave the tcgen05 kernel through shared
+    memory and TMA stores when the output's base and row pitch are 16-byte
+    aligned, and through plain per-row stores otherwise (and for the ragged
+    last tile of a sequence).  An output view one element off alignment, and
+    one with a wider row pitch, must hold the same bits as a dense output,
+    and the bytes around the view must stay untouched."""
+    ops = _ops()
+    H, kv, D = 32, 8, 128
+    lens = [1024, 300, 129, 128]
+    g = torch.Generator(device=cuda).manual_seed(41)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32).to(cuda)
+    T = sum(lens)
+    q = torch.randn(T, H, D, device=cuda, generator=g).to(torch.bfloat16)
+    k = torch.randn(T, kv, D, device=cuda, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, kv, D, device=cuda, generator=g).to(torch.bfloat16)
+    dense = ops.prefill_attention(q, k, v, cu, max(lens))
+    for pad_front, pitch in ((1, H * D), (0, H * D + 64)):
+        buf = torch.full((T * pitch + pad_front + 64,), 7.0, device=cuda, dtype=torch.bfloat16)
+        view = buf[pad_front:pad_front + T * pitch].view(T, pitch)[:, :H * D].view(T, H, D)
+        ops.prefill_attention(q, k, v, cu, max(lens), out=view)
+        assert ops.device_errors() == 0
+        assert torch.equal(view.view(torch.int16), dense.view(torch.int16)), (pad_front, pitch)
+        rows = buf[pad_front:pad_front + T * pitch].view(T, pitch)
+        assert (rows[:, H * D:] == 7).all() and (buf[:pad_front] == 7).all()
+        assert (buf[pad_front + T * pitch:] == 7).all()
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 def test_swap_kv_blocks_round_trip(cuda, dt):
     """Swap-out to a pinned host cache and swap-in to other device blocks,
