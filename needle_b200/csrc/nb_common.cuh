@@ -310,6 +310,18 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                    bar)
                : "memory");
 }
+// One lane of the (converged) warp: true in exactly one thread.  The warp
+// runs the issuing loop together, so its operands stay warp-uniform, and the
+// elected lane issues the single-thread tcgen05 instructions.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r));
+  return r != 0;
+}
 // D[tmem] (+)= A[smem desc] * B[smem desc]; one thread issues it.
 __device__ __forceinline__ void tc_mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                               uint32_t idesc, uint32_t accumulate) {

@@ -346,30 +346,40 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
         mbar_wait_bounded(bar_v + 8 * (i & 1), (i >> 1) & 1);
     }
   } else if (warp == kPf3WarpMma) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer: the whole warp runs the loop, one elected
+    // lane issues each MMA and commit ----------------
+    {
       uint32_t nq = 0, nk = 0, nv = 0;           // tiles consumed (running counts)
       uint32_t np[2] = {0, 0}, no[2] = {0, 0};   // P tiles consumed, units finished per group
       bool ok = true;
       auto wait = [&](uint32_t bar, uint32_t par) {
         if (!ok) return false;
-        if (*abort_flag || !mbar_wait_bounded(bar, par)) ok = false;
+        // one answer for the warp, which takes every branch together
+        ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait_bounded(bar, par));
         return ok;
       };
+      auto commit = [&](uint32_t bar) {
+        if (elect_one()) tc_commit(bar);
+      };
       auto issue_s = [&](uint32_t q_off, uint32_t kst, uint32_t t_col) {
+        const bool leader = elect_one();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * G::kAtom + (kk & 3) * 32;
-          tc_mma_f16_ss(tmem + t_col, smem_desc_sw128(sb + q_off + off, 16, 1024),
-                        smem_desc_sw128(kst + off, 16, 1024), kIdS, kk > 0);
+          const uint64_t ad = smem_desc_sw128(sb + q_off + off, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(kst + off, 16, 1024);
+          if (leader) tc_mma_f16_ss(tmem + t_col, ad, bd, kIdS, kk > 0);
         }
       };
       auto issue_pv = [&](uint32_t vst, uint32_t s_col, uint32_t o_col, bool first) {
+        const bool leader = elect_one();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc_mma_f16_ts(tmem + o_col, tmem + s_col + kk * 8,
-                        smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024), kIdO,
-                        (!first || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t bd = smem_desc_sw128(vst + kk * 16 * 128, G::kAtom, 1024);
+          if (leader)
+            tc_mma_f16_ts(tmem + o_col, tmem + s_col + kk * 8, bd, kIdO,
+                          (!first || kk > 0) ? 1u : 0u);
+        }
       };
       // the first unit at or after round rd with work (its KV tile counts)
       auto next_unit = [&](int& rd, int& tA, int& tB) -> bool {
@@ -402,10 +412,10 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
           for (int x = 0; x < 2; ++x) {
             if (!nx[x]) continue;
             issue_s(qoff[x], sb + G::kK + st * G::kTile, scol[x]);
-            tc_commit(bar_s + 8 * x);
+            commit(bar_s + 8 * x);
           }
-          tc_commit(bar_kfree + 8 * st);
-          if (n_kv == 1) tc_commit(bar_qfree);
+          commit(bar_kfree + 8 * st);
+          if (n_kv == 1) commit(bar_qfree);
           ++nk;
           first_unit = false;
         }
@@ -441,7 +451,7 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
             tc_fence_after();
             issue_pv(sb + G::kV + vst * G::kTile, scol[x], ocol[x], j == 0);
             if (j + 1 == nx[x]) {
-              tc_commit(bar_o + 8 * x);  // O_X final for this unit
+              commit(bar_o + 8 * x);  // O_X final for this unit
               ++no[x];
               // At the unit's last KV tile the next unit's S_X(0) goes in
               // right behind this P.V, before the other tile's P is waited
@@ -451,7 +461,7 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
               if (have2 && mx[x] && !has_next) {
                 if (!next_ready()) break;
                 issue_s(qoff[x], sb + G::kK + (nk & 1) * G::kTile, scol[x]);
-                tc_commit(bar_s + 8 * x);  // also covers P_X(j).V_j
+                commit(bar_s + 8 * x);  // also covers P_X(j).V_j
                 early |= 1u << x;
               }
             } else {
@@ -461,15 +471,15 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
                 k_ready = true;
               }
               issue_s(qoff[x], sb + G::kK + kst * G::kTile, scol[x]);
-              tc_commit(bar_s + 8 * x);  // also covers P_X(j).V_j
+              commit(bar_s + 8 * x);  // also covers P_X(j).V_j
             }
           }
           if (!ok) break;
-          tc_commit(bar_vfree + 8 * vst);
+          commit(bar_vfree + 8 * vst);
           ++nv;
           if (has_next) {
-            tc_commit(bar_kfree + 8 * kst);
-            if (j + 2 == n_kv) tc_commit(bar_qfree);  // last S MMAs of the unit issued
+            commit(bar_kfree + 8 * kst);
+            if (j + 2 == n_kv) commit(bar_qfree);  // last S MMAs of the unit issued
             ++nk;
           }
         }
@@ -482,11 +492,11 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
           for (int x = 0; x < 2; ++x) {
             if (!mx[x] || ((early >> x) & 1u)) continue;
             issue_s(qoff[x], sb + G::kK + (nk & 1) * G::kTile, scol[x]);
-            tc_commit(bar_s + 8 * x);
+            commit(bar_s + 8 * x);
           }
           ++nq;
-          tc_commit(bar_kfree + 8 * (nk & 1));
-          if ((mB ? mB : mA) == 1) tc_commit(bar_qfree);
+          commit(bar_kfree + 8 * (nk & 1));
+          if ((mB ? mB : mA) == 1) commit(bar_qfree);
           ++nk;
         }
         rd = rd2;
@@ -494,11 +504,11 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
         nB = mB;
         have = have2;
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         *abort_flag = 1;
         set_error(kErrTimeout);
       }
-      tc_commit(bar_end);
+      commit(bar_end);
       mbar_wait_bounded(bar_end, 0);  // every MMA issued by this CTA has finished
     }
   }

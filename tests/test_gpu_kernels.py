@@ -516,32 +516,56 @@ def test_prefill_many_units_per_cta(cuda, lens):
     assert err <= 2e-2, err
 
 
-def test_prefill_output_store_paths_agree(cuda):
+_STORE_PATH_CHECK = r"""
+import sys
+import numpy as np
+import torch
+from needle_b200 import ops
+dev = torch.device("cuda:0")
+H, kv, D = 32, 8, 128
+lens = [1024, 300, 129, 128]
+g = torch.Generator(device=dev).manual_seed(41)
+cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32).to(dev)
+T = sum(lens)
+q = torch.randn(T, H, D, device=dev, generator=g).to(torch.bfloat16)
+k = torch.randn(T, kv, D, device=dev, generator=g).to(torch.bfloat16)
+v = torch.randn(T, kv, D, device=dev, generator=g).to(torch.bfloat16)
+dense = ops.prefill_attention(q, k, v, cu, max(lens))
+# a wider row pitch (still 16-byte aligned: the tensor-core kernel takes it)
+pitch = H * D + 64
+buf = torch.full((T * pitch + 64,), 7.0, device=dev, dtype=torch.bfloat16)
+rows = buf[:T * pitch].view(T, pitch)
+view = rows[:, :H * D].view(T, H, D)
+ops.prefill_attention(q, k, v, cu, max(lens), out=view)
+assert ops.device_errors() == 0
+assert torch.equal(view.view(torch.int16), dense.view(torch.int16))
+assert (rows[:, H * D:] == 7).all() and (buf[T * pitch:] == 7).all()
+dense.view(torch.int16).cpu().numpy().tofile(sys.argv[1])
+print("ok")
+"""
+
+
+def test_prefill_output_store_paths_agree(cuda, tmp_path):
     """Whole 128-row output tiles leave the tcgen05 kernel through shared
-    memory and TMA stores when the output's base and row pitch are 16-byte
-    aligned, and through plain per-row stores otherwise (and for the ragged
-    last tile of a sequence).  An output view one element off alignment, and
-    one with a wider row pitch, must hold the same bits as a dense output,
-    and the bytes around the view must stay untouched."""
-    ops = _ops()
-    H, kv, D = 32, 8, 128
-    lens = [1024, 300, 129, 128]
-    g = torch.Generator(device=cuda).manual_seed(41)
-    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32).to(cuda)
-    T = sum(lens)
-    q = torch.randn(T, H, D, device=cuda, generator=g).to(torch.bfloat16)
-    k = torch.randn(T, kv, D, device=cuda, generator=g).to(torch.bfloat16)
-    v = torch.randn(T, kv, D, device=cuda, generator=g).to(torch.bfloat16)
-    dense = ops.prefill_attention(q, k, v, cu, max(lens))
-    for pad_front, pitch in ((1, H * D), (0, H * D + 64)):
-        buf = torch.full((T * pitch + pad_front + 64,), 7.0, device=cuda, dtype=torch.bfloat16)
-        view = buf[pad_front:pad_front + T * pitch].view(T, pitch)[:, :H * D].view(T, H, D)
-        ops.prefill_attention(q, k, v, cu, max(lens), out=view)
-        assert ops.device_errors() == 0
-        assert torch.equal(view.view(torch.int16), dense.view(torch.int16)), (pad_front, pitch)
-        rows = buf[pad_front:pad_front + T * pitch].view(T, pitch)
-        assert (rows[:, H * D:] == 7).all() and (buf[:pad_front] == 7).all()
-        assert (buf[pad_front + T * pitch:] == 7).all()
+    memory and TMA stores; the ragged last tile of a sequence, and every tile
+    with NB_PF3_TMA_STORE=0, through plain per-row 16-byte stores.  Both
+    runs (fresh processes) must give the same bits, for a dense output and
+    for one with a wider row pitch, whose padding stays untouched.  (An
+    output that is not 16-byte aligned never reaches this kernel: the
+    library takes its SIMT prefill then.)"""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    outs = []
+    for flag in ("1", "0"):
+        f = tmp_path / f"out{flag}.bin"
+        env = dict(os.environ, NB_PF3_TMA_STORE=flag)
+        r = subprocess.run([sys.executable, "-c", _STORE_PATH_CHECK, str(f)], cwd=root, env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+        outs.append(f.read_bytes())
+    assert outs[0] == outs[1]
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
