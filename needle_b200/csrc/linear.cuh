@@ -170,17 +170,21 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         mbar_wait_bounded(bar_full + 8 * (j % kStages), (j / kStages) & 1);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: the whole warp runs the loop (operands
+    // warp-uniform), one elected lane issues each MMA and commit ----------------
     griddep_wait();  // the bounded waits below start once the previous kernel is done
-    if (lane == 0) {
+    {
       const uint32_t idesc = idesc_f16_f32(kBf16, 128, NT, false, false);
       uint32_t it = 0;
       int i = 0;
       bool ok = true;
+      // one answer for the warp, which takes every branch together
+      auto wait = [&](uint32_t bar, uint32_t par) {
+        return __all_sync(0xffffffffu, !*abort_flag && mbar_wait_bounded(bar, par));
+      };
       for (int t = tile0; ok && t < n_tiles; t += tstep, ++i) {
         const int buf = i % kNbuf, use = i / kNbuf;
-        if (use > 0 &&
-            (*abort_flag || !mbar_wait_bounded(bar_accfree + 8 * buf, (use & 1) ^ 1))) {
+        if (use > 0 && !wait(bar_accfree + 8 * buf, (use & 1) ^ 1)) {
           ok = false;
           break;
         }
@@ -188,29 +192,32 @@ __global__ void __launch_bounds__(kLinThreads, 1)
         const uint32_t d = tmem + buf * TW * acc_cols;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const uint32_t st = it % kStages, round = it / kStages;
-          if (*abort_flag || !mbar_wait_bounded(bar_full + 8 * st, round & 1)) {
+          if (!wait(bar_full + 8 * st, round & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a = sb + st * kStage, b = a + TW * kLinW;
+          const bool leader = elect_one();
 #pragma unroll
           for (int w = 0; w < TW; ++w)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc_mma_f16_ss(d + w * acc_cols, smem_desc_sw128(a + w * kLinW + kk * 32, 16, 1024),
-                            smem_desc_sw128(b + kk * 32, 16, 1024), idesc,
-                            (kb > kb0 || kk > 0) ? 1u : 0u);
-          tc_commit(bar_empty + 8 * st);  // the stage may be refilled
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = smem_desc_sw128(a + w * kLinW + kk * 32, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(b + kk * 32, 16, 1024);
+              if (leader)
+                tc_mma_f16_ss(d + w * acc_cols, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
+          if (leader) tc_commit(bar_empty + 8 * st);  // the stage may be refilled
         }
         if (!ok) break;
-        tc_commit(bar_acc + 8 * buf);
+        if (elect_one()) tc_commit(bar_acc + 8 * buf);
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         *abort_flag = 1;
         set_error(kErrTimeout);
       }
-      tc_commit(bar_end);
+      if (elect_one()) tc_commit(bar_end);
       mbar_wait_bounded(bar_end, 0);
     }
   } else {

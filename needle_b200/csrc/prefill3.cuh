@@ -263,31 +263,38 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
   if (wg == 3) {
     setmaxnreg_dec<kPf3IssueRegs>();
   if (warp == kPf3WarpTma) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
+    // ---------------- TMA producer: the whole warp runs the loop, one
+    // elected lane issues the copies ----------------
+    {
       uint32_t nq = 0, nk = 0, nv = 0;  // loads issued (running counts)
       bool ok = true;
+      // one answer for the warp, which takes every branch together
+      auto wait = [&](uint32_t bar, uint32_t par) {
+        return __all_sync(0xffffffffu, mbar_wait_bounded(bar, par));
+      };
       for (int rd = 0, u = unit_of(0); ok && u < n_units; u = unit_of(++rd)) {
         const Pf3Unit w = pf3_unit(u, hq, B, nqb, pair);
         int s0, len, nA, nB, c;
         if (!extent(w, s0, len, nA, nB, c)) continue;
         const int kh = w.h / group;
         const int n_kv = nB ? nB : nA;
-        if (nq > 0 && !mbar_wait_bounded(bar_qfree, (nq - 1) & 1)) { ok = false; break; }
-        mbar_arrive_expect_tx(bar_q, (nB ? 2 : 1) * G::kTile);
+        if (nq > 0 && !wait(bar_qfree, (nq - 1) & 1)) { ok = false; break; }
+        if (elect_one()) {
+          mbar_arrive_expect_tx(bar_q, (nB ? 2 : 1) * G::kTile);
 #pragma unroll
-        for (int a = 0; a < D / 64; ++a) {
-          tma_load_2d(sb + G::kQA + a * G::kAtom, &qmap, pf3_head(w, 0, pair) * D + a * 64,
-                      s0 + pf3_row(w, 0, pair), bar_q);
-          if (nB)
-            tma_load_2d(sb + G::kQB + a * G::kAtom, &qmap, pf3_head(w, 1, pair) * D + a * 64,
-                        s0 + pf3_row(w, 1, pair), bar_q);
+          for (int a = 0; a < D / 64; ++a) {
+            tma_load_2d(sb + G::kQA + a * G::kAtom, &qmap, pf3_head(w, 0, pair) * D + a * 64,
+                        s0 + pf3_row(w, 0, pair), bar_q);
+            if (nB)
+              tma_load_2d(sb + G::kQB + a * G::kAtom, &qmap, pf3_head(w, 1, pair) * D + a * 64,
+                          s0 + pf3_row(w, 1, pair), bar_q);
+          }
         }
         ++nq;
         for (int j = 0; j < n_kv; ++j) {
-          if (*abort_flag) { ok = false; break; }
+          if (__any_sync(0xffffffffu, *abort_flag)) { ok = false; break; }
           const uint32_t st = nk & 1;
-          if (nk >= 2 && !mbar_wait_bounded(bar_kfree + 8 * st, ((nk >> 1) - 1) & 1)) {
+          if (nk >= 2 && !wait(bar_kfree + 8 * st, ((nk >> 1) - 1) & 1)) {
             ok = false;
             break;
           }
@@ -300,40 +307,44 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
             for (int pp = 0; pp < 8; ++pp) prow[pp] = page_row(w.b, j * 8 + pp, kh);
           }
           const int v_off = paged ? pg.num_blocks * pg.kvh * 16 : 0;
-          mbar_arrive_expect_tx(bar_k + 8 * st, G::kTile);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(bar_k + 8 * st, G::kTile);
 #pragma unroll
-          for (int a = 0; a < D / 64; ++a) {
-            const uint32_t dst = sb + G::kK + st * G::kTile + a * G::kAtom;
-            if (paged) {
+            for (int a = 0; a < D / 64; ++a) {
+              const uint32_t dst = sb + G::kK + st * G::kTile + a * G::kAtom;
+              if (paged) {
 #pragma unroll
-              for (int pp = 0; pp < 8; ++pp)
-                tma_load_2d(dst + pp * 16 * 128, &kmap, a * 64, prow[pp], bar_k + 8 * st);
-            } else {
-              tma_load_2d(dst, &kmap, kh * D + a * 64, s0 + j * 128, bar_k + 8 * st);
+                for (int pp = 0; pp < 8; ++pp)
+                  tma_load_2d(dst + pp * 16 * 128, &kmap, a * 64, prow[pp], bar_k + 8 * st);
+              } else {
+                tma_load_2d(dst, &kmap, kh * D + a * 64, s0 + j * 128, bar_k + 8 * st);
+              }
             }
           }
           ++nk;
-          if (nv >= 2 && !mbar_wait_bounded(bar_vfree + 8 * st, ((nv >> 1) - 1) & 1)) {
+          if (nv >= 2 && !wait(bar_vfree + 8 * st, ((nv >> 1) - 1) & 1)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(bar_v + 8 * st, G::kTile);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(bar_v + 8 * st, G::kTile);
 #pragma unroll
-          for (int a = 0; a < D / 64; ++a) {
-            const uint32_t dst = sb + G::kV + st * G::kTile + a * G::kAtom;
-            if (paged) {
+            for (int a = 0; a < D / 64; ++a) {
+              const uint32_t dst = sb + G::kV + st * G::kTile + a * G::kAtom;
+              if (paged) {
 #pragma unroll
-              for (int pp = 0; pp < 8; ++pp)
-                tma_load_2d(dst + pp * 16 * 128, &kmap, a * 64,
-                            prow[pp] < 0 ? prow[pp] : prow[pp] + v_off, bar_v + 8 * st);
-            } else {
-              tma_load_2d(dst, &vmap, kh * D + a * 64, s0 + j * 128, bar_v + 8 * st);
+                for (int pp = 0; pp < 8; ++pp)
+                  tma_load_2d(dst + pp * 16 * 128, &kmap, a * 64,
+                              prow[pp] < 0 ? prow[pp] : prow[pp] + v_off, bar_v + 8 * st);
+              } else {
+                tma_load_2d(dst, &vmap, kh * D + a * 64, s0 + j * 128, bar_v + 8 * st);
+              }
             }
           }
           ++nv;
         }
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         *abort_flag = 1;
         set_error(kErrTimeout);
       }
