@@ -37,31 +37,39 @@
 // MMAs, then tensor memory is freed.
 #pragma once
 #include <climits>
+#include <type_traits>
 
 #include "nb_common.cuh"
 
 namespace nb {
 
-// 2^x on the FMA/ALU pipes, for the share of the softmax exponentials that
-// would otherwise queue on the MUFU (XU) pipe, which limits this kernel.
-// Cody-Waite style range reduction: n = round(x) through the 1.5 * 2^23 magic
-// constant, f = x - n in [-0.5, 0.5]; 2^f by a cubic whose coefficients were
-// fit here (least squares weighted by relative error on [-0.5, 0.5], maximum
-// relative error 1.0e-4, below half a unit of bf16 and fp16); 2^n is added to
-// the exponent field.  Valid for x >= -126 (the unmasked scores, which are at
-// most a few units above the running max).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = __fadd_rn(x, 12582912.f);
-  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
-  float p = fmaf(0.05500858144334074f, f, 0.24221037434204812f);
-  p = fmaf(p, f, 0.6932829004942702f);
-  p = fmaf(p, f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// 2^x for two values on the FMA/ALU pipes (packed fp32 pairs), for a share
+// of the softmax exponentials that would otherwise queue on the MUFU (XU)
+// pipe.  Cody-Waite style range reduction: n = round(x) through the
+// 1.5 * 2^23 magic constant, f = x - n in [-0.5, 0.5] (formed as n * -1 + x,
+// one rounding as a subtraction); 2^f by a cubic whose coefficients were fit
+// here (least squares weighted by relative error on [-0.5, 0.5], maximum
+// relative error 1.0e-4, below half a unit of bf16 and fp16); 2^n is added
+// to the exponent field.  Valid for x >= -126 (the unmasked scores, which
+// are at most a few units above the running max).
+__device__ __forceinline__ void exp2_poly2(float& y0, float& y1, float x0, float x1) {
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float t0, t1, n0, n1, f0, f1, p0, p1;
+  add_f32x2(t0, t1, x0, x1, 12582912.f, 12582912.f);
+  add_f32x2(n0, n1, t0, t1, -12582912.f, -12582912.f);
+  fma_f32x2(f0, f1, n0, n1, -1.f, -1.f, x0, x1);
+  fma_f32x2(p0, p1, f0, f1, 0.05500858144334074f, 0.05500858144334074f, 0.24221037434204812f,
+            0.24221037434204812f);
+  fma_f32x2(p0, p1, p0, p1, f0, f1, 0.6932829004942702f, 0.6932829004942702f);
+  fma_f32x2(p0, p1, p0, p1, f0, f1, 1.0f, 1.0f);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-// Exponentials per group of 8 value pairs that take exp2_poly instead of
-// the MUFU in unmasked tiles.
+// Value pairs (of every 8) that take exp2_poly2 instead of the MUFU in a
+// warp whose rows are all unmasked; 0 by default (measured slower: the
+// softmax warps spill at 168 registers with both paths in the loop).
 #ifndef NB_PF3_POLY
 #define NB_PF3_POLY 0
 #endif
@@ -592,34 +600,43 @@ __global__ void __launch_bounds__(kPf3Threads, 1)
         const float neg_m = -m;
         // row sum in 4 independent partials of (even, odd) column pairs
         float rsa[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+        // exponentials, row sums and P; `kPoly` (a warp whose rows are all
+        // unmasked in this tile) takes exp2_poly2 for the first NB_PF3_POLY
+        // of every 8 value pairs
+        auto exp_tile = [&](auto poly_tag) {
+          constexpr bool kPoly = decltype(poly_tag)::value;
 #pragma unroll
-        for (int c = 0; c < NCC; ++c) {
+          for (int c = 0; c < NCC; ++c) {
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t pk[8];
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t pk[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              // masked scores are -inf: the MUFU's exp2 gives exactly 0, so
-              // masked tiles use it for every value
-              const int i = hh * 16 + 2 * e;
-              float x0, x1;
-              fma_f32x2(x0, x1, __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
-                        scale_log2, scale_log2, neg_m, neg_m);
-              float p0, p1;
-              if (e < NB_PF3_POLY && full) {
-                p0 = exp2_poly(x0);
-                p1 = exp2_poly(x1);
-              } else {
-                p0 = ex2_approx(x0);
-                p1 = ex2_approx(x1);
+              for (int e = 0; e < 8; ++e) {
+                // masked scores are -inf: the MUFU's exp2 gives exactly 0, so
+                // tiles with masked rows use it for every value
+                const int i = hh * 16 + 2 * e;
+                float x0, x1;
+                fma_f32x2(x0, x1, __uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
+                          scale_log2, scale_log2, neg_m, neg_m);
+                float p0, p1;
+                if (kPoly && e < NB_PF3_POLY) {
+                  exp2_poly2(p0, p1, x0, x1);
+                } else {
+                  p0 = ex2_approx(x0);
+                  p1 = ex2_approx(x1);
+                }
+                add_f32x2(rsa[e & 3][0], rsa[e & 3][1], rsa[e & 3][0], rsa[e & 3][1], p0, p1);
+                pk[e] = Mma<T>::pack(p0, p1);
               }
-              add_f32x2(rsa[e & 3][0], rsa[e & 3][1], rsa[e & 3][0], rsa[e & 3][1], p0, p1);
-              pk[e] = Mma<T>::pack(p0, p1);
+              // P over S's first 64 columns
+              tmem_st8(tS + lane_off + c * 16 + hh * 8, pk);
             }
-            // P over S's first 64 columns
-            tmem_st8(tS + lane_off + c * 16 + hh * 8, pk);
           }
-        }
+        };
+        if (NB_PF3_POLY > 0 && __all_sync(0xffffffffu, full))
+          exp_tile(std::true_type{});
+        else
+          exp_tile(std::false_type{});
         add_f32x2(rsa[0][0], rsa[0][1], rsa[0][0], rsa[0][1], rsa[1][0], rsa[1][1]);
         add_f32x2(rsa[2][0], rsa[2][1], rsa[2][0], rsa[2][1], rsa[3][0], rsa[3][1]);
         const float rs = (rsa[0][0] + rsa[2][0]) + (rsa[0][1] + rsa[2][1]);
