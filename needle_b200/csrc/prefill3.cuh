@@ -15,8 +15,9 @@
 //   * Sixteen warps in four warpgroups: warps 0-3 and 4-7 run the softmax of
 //     tiles A and B (thread = query row = TMEM lane; warp w reaches lanes
 //     32 (w mod 4) .. +31), warps 8-11 write out O (the epilogue), warp 12
-//     issues TMA loads, warp 13 issues the MMAs (one lane), warps 14-15 only
-//     take part in the register split.  `setmaxnreg` moves registers from the
+//     issues TMA loads and warp 13 the MMAs (each runs its loop warp-wide,
+//     so the operands stay warp-uniform, and one elected lane issues),
+//     warps 14-15 only take part in the register split.  `setmaxnreg` moves registers from the
 //     epilogue and issuing warpgroups to the softmax warpgroups, which hold a
 //     row's 128 scores in registers.  K and V have separate two-stage rings
 //     with their own "free" barriers: K_j is released as soon as both S MMAs
