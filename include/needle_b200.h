@@ -218,6 +218,10 @@ NB_API int nb_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t 
  * [T, Hq, D].  Replaces needle/layers/attention.py:120-134 (_prefill_pytorch)
  * and :109-118 (_prefill_flashinfer): within sequence s token i attends to
  * tokens 0..i of the same sequence, query head j to KV head j / group.
+ * bf16 / fp16 with head_dim 64 or 128, 16-byte aligned q, k, v and out and
+ * row strides of a multiple of 16 bytes run on the tcgen05 kernel; anything
+ * else (fp32, other head dims, unaligned rows) runs a slower SIMT kernel with
+ * the same semantics.
  */
 NB_API int nb_prefill_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                          const void* v, int64_t v_stride, int num_q_heads, int num_kv_heads,
